@@ -1,0 +1,140 @@
+/*
+ * vf_b200 — C ABI of the sm_100a relative-position encoder attention kernels.
+ *
+ * Plain pointers, sizes and strides only; no torch types cross this boundary.  All
+ * tensor pointers are DEVICE pointers on the current CUDA device; `stream` is a
+ * cudaStream_t (NULL = legacy default stream).  Every entry point returns 0 on success
+ * or a negative VF_E* code; vf_last_error() then holds a one-line message for the
+ * calling thread.  Nothing here allocates device memory: callers own every buffer.
+ *
+ * The reference (vllm-factory 0.2.2) has no native layer: its two hot-path operators
+ * are Python launchers of Triton kernels.  Each entry point below names the Python
+ * interface it replaces, and the ctypes binding in vllm-factory_b200/vf_b200/_lib.py is
+ * the binding a maintainer of the reference would add.
+ */
+#ifndef VF_B200_H_
+#define VF_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VF_ABI_VERSION 1
+
+/* Error codes. */
+#define VF_OK 0
+#define VF_EINVAL (-1)       /* bad shape, stride, dtype or argument value            */
+#define VF_EUNSUPPORTED (-2) /* valid for the reference but not implemented here     */
+#define VF_ECUDA (-3)        /* a CUDA runtime / driver call failed                  */
+
+typedef enum {
+  VF_DTYPE_F32 = 0,
+  VF_DTYPE_F16 = 1,
+  VF_DTYPE_BF16 = 2,
+} vf_dtype_t;
+
+/* A rank-4 strided view.  Strides are in ELEMENTS.  data == NULL means "absent". */
+typedef struct {
+  const void* data;
+  int64_t size[4];
+  int64_t stride[4];
+} vf_tensor4d_t;
+
+/* ------------------------------------------------------------------------------------
+ * T5 relative-position-bias attention (mT5 encoder self-attention).
+ * Replaces kernels/flash_attention_rpb.py:296 `flash_attention_rpb_final(q, k, v,
+ * rpb_table, num_buckets, max_distance, is_decoder, padding_mask=None, dropout_p=0.0,
+ * softmax_scale=1.0, use_autotune=True)` and its kernel (:62-230).
+ *
+ *   out[b,h,m,:] = softmax_n( scale * q[b,h,m]·k[b,h,n]
+ *                              + rpb_table[bucket(n - m), h] + padding_mask[b,h,m,n] ) v[b,h,n,:]
+ *
+ * q, k, v, out: (B, H, M|N, 64), dtype 16-bit (f16/bf16), innermost stride 1.
+ * rpb_table: (num_table_rows, H) 2-D with the given element strides, or NULL (no bias).
+ * padding_mask: additive, broadcastable (B|1, H|1, 1, N); data NULL = none.
+ * Rows of a batch whose padding mask is <= -1e4 on every key of a 128-key tile make
+ * that tile contribute exactly zero, so such tiles at either end are skipped.
+ * ------------------------------------------------------------------------------------ */
+typedef struct {
+  vf_dtype_t dtype;
+  vf_tensor4d_t q, k, v;
+  vf_tensor4d_t out;
+  const void* rpb_table;
+  int64_t table_rows, table_cols;
+  int64_t table_stride_row, table_stride_col;
+  vf_dtype_t table_dtype;
+  int32_t num_buckets;
+  int32_t max_distance;
+  int32_t is_decoder;
+  vf_tensor4d_t padding_mask;
+  vf_dtype_t mask_dtype;
+  float dropout_p;
+  float softmax_scale;
+} vf_rpb_attention_args_t;
+
+int vf_rpb_attention_fwd(const vf_rpb_attention_args_t* args, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * DeBERTa disentangled attention (c2p + p2c relative-position scores).
+ * Replaces kernels/flash_deberta_attention.py:455 `flash_deberta_attention(q, k, v,
+ * seq_lengths=None, pos_key=None, pos_query=None, causal=False, sm_scale=None,
+ * position_buckets=0, max_relative_distance=0, use_log_bucket=False)` and its Triton
+ * launcher/kernel (:306-372, :145-299).
+ *
+ *   idx(m, n) = clamp(bucket(m - n) + S, 0, 2S - 1),   S = position_buckets or max_rel
+ *   s[m, n]   = sm_scale * (q[m]·k[n] + pos_key[m, idx] + pos_query[n, idx])
+ *   out[m]    = softmax over keys n < seq_len(b) of s, times v;  rows m >= seq_len -> 0
+ *
+ * q, out: (B, H, M, 64); k, v: (B, H, N, 64); 16-bit dtype; innermost stride 1.
+ * pos_key: (B, H, M, 2S), pos_query: (B, H, N, 2S), same dtype as q; NULL = term absent.
+ * seq_lengths: device int32 (B,) or NULL (all rows/keys valid).
+ * has_sm_scale == 0 selects the reference default 1/sqrt(head_dim).
+ * ------------------------------------------------------------------------------------ */
+typedef struct {
+  vf_dtype_t dtype;
+  vf_tensor4d_t q, k, v;
+  vf_tensor4d_t out;
+  const int32_t* seq_lengths;
+  vf_tensor4d_t pos_key, pos_query;
+  int32_t causal;
+  int32_t has_sm_scale;
+  float sm_scale;
+  int32_t position_buckets;
+  int32_t max_relative_distance;
+  int32_t use_log_bucket;
+} vf_deberta_attention_args_t;
+
+int vf_deberta_attention_fwd(const vf_deberta_attention_args_t* args, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Host-side bucket functions (no GPU needed).  These are the exact integer outputs the
+ * kernels use; they restate, in float32 arithmetic like the reference's torch code:
+ *  - models/mt5/mt5_encoder.py:125 T5RelativePositionBias._relative_position_bucket
+ *    (also the in-kernel copy kernels/flash_attention_rpb.py:13 _get_rp_bucket);
+ *  - models/deberta_v2/deberta_v2_encoder.py:70 make_log_bucket_position (also the
+ *    in-kernel copy kernels/flash_deberta_attention.py:234-243).
+ * They fill out[i] for relative positions r = rmin + i, i in [0, rmax - rmin].
+ * ------------------------------------------------------------------------------------ */
+int vf_t5_relative_bucket(int32_t num_buckets, int32_t max_distance, int32_t bidirectional,
+                          int32_t rmin, int32_t rmax, int32_t* out);
+int vf_deberta_log_bucket(int32_t bucket_size, int32_t max_position,
+                          int32_t rmin, int32_t rmax, int32_t* out);
+
+/* Thread-local message for the last failing call on this thread ("" if none). */
+const char* vf_last_error(void);
+
+/* Reads (and optionally clears) the device error word of the current device: bit 0 = a
+ * bounded in-kernel wait ran out of time, bit 1 = a gather index failed its bounds check.
+ * Synchronises the device.  Returns the word (>= 0) or VF_ECUDA. */
+int vf_device_error(int32_t clear);
+
+/* VF_ABI_VERSION of the loaded library. */
+int vf_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VF_B200_H_ */

@@ -1,0 +1,151 @@
+"""GPU parity of the T5-RPB attention op (kernels.flash_attention_rpb drop-in) against the
+CPU oracle (fp64) and the reference's golden outputs.  Gates: max-abs <= 2e-2 and per-row
+cosine >= 0.9999."""
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as gi
+import oracle
+from _util import assert_close, lens_mask
+
+pytestmark = pytest.mark.gpu
+
+
+def _import_op():
+    from kernels.flash_attention_rpb import flash_attention_rpb_final
+    return flash_attention_rpb_final
+
+
+def make_inputs(B, H, M, N, dtype, lens=None, nb=32, seed=0, per_head_mask=False):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, M, 64, generator=g).to(dtype)
+    k = torch.randn(B, H, N, 64, generator=g).to(dtype)
+    v = torch.randn(B, H, N, 64, generator=g).to(dtype)
+    table = (torch.randn(nb, H, generator=g) * 2.0).to(dtype)
+    mask = None
+    if lens is not None:
+        m = (torch.arange(N)[None, :] < torch.tensor(lens)[:, None]).to(dtype)
+        mask = ((1.0 - m[:, None, None, :].float()) * torch.finfo(dtype).min).to(dtype)
+        if per_head_mask:
+            mask = mask.expand(B, H, 1, N).contiguous()
+            mask[:, 1::2, :, :2] = torch.finfo(dtype).min   # heads differ
+    return q, k, v, table, mask
+
+
+def check(q, k, v, table, mask, nb=32, md=128, is_decoder=False, scale=1.0, what=""):
+    op = _import_op()
+    dev = torch.device("cuda")
+    out = op(q.to(dev), k.to(dev), v.to(dev), None if table is None else table.to(dev), nb, md, is_decoder,
+             None if mask is None else mask.to(dev), 0.0, scale)
+    torch.cuda.synchronize()
+    ref = oracle.rpb_attention_ref(q.float(), k.float(), v.float(), None if table is None else table.float(),
+                                   nb, md, is_decoder, None if mask is None else mask.float(), scale)
+    assert out.shape == q.shape and out.dtype == q.dtype
+    assert torch.isfinite(out.float()).all(), f"{what}: non-finite output"
+    return assert_close(out, ref, None, what=what)
+
+
+@pytest.mark.parametrize("M", [1, 64, 128, 129, 200, 256, 300, 513])
+def test_rpb_lengths(M):
+    q, k, v, t, m = make_inputs(2, 2, M, M, torch.bfloat16, lens=[M, max(1, M // 2)], seed=M)
+    check(q, k, v, t, m, what=f"M={M}")
+
+
+def test_rpb_no_mask_no_table():
+    q, k, v, _, _ = make_inputs(1, 3, 384, 384, torch.bfloat16, seed=5)
+    check(q, k, v, None, None, what="plain")
+
+
+def test_rpb_fp16_and_scale():
+    q, k, v, t, m = make_inputs(2, 2, 320, 320, torch.float16, lens=[320, 33], seed=6)
+    check(q, k, v, t, m, scale=0.125, what="fp16")
+
+
+def test_rpb_cross_lengths():
+    q, k, v, t, m = make_inputs(2, 2, 160, 400, torch.bfloat16, lens=[400, 250], seed=7)
+    check(q, k, v, t, m, what="M!=N")
+
+
+def test_rpb_per_head_mask():
+    q, k, v, t, m = make_inputs(2, 4, 256, 256, torch.bfloat16, lens=[256, 100], seed=8, per_head_mask=True)
+    check(q, k, v, t, m, what="per-head mask")
+
+
+def test_rpb_decoder_causal():
+    q, k, v, t, m = make_inputs(2, 2, 300, 300, torch.bfloat16, lens=[300, 280], seed=9)
+    check(q, k, v, t, m, is_decoder=True, what="decoder")
+
+
+def test_rpb_other_bucket_configs():
+    q, k, v, t, m = make_inputs(1, 2, 700, 700, torch.bfloat16, lens=[650], nb=64, seed=10)
+    check(q, k, v, t, m, nb=64, md=256, what="64/256")
+
+
+def test_rpb_fully_masked_batch_is_uniform_average():
+    # Every key masked: the reference softmax degenerates to a uniform average over keys.
+    q, k, v, t, m = make_inputs(2, 2, 130, 130, torch.bfloat16, lens=[130, 0], seed=11)
+    check(q, k, v, t, m, what="fully masked")
+
+
+def test_rpb_noncontiguous_views_and_sliced_table():
+    B, H, L = 2, 4, 256
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(B, L, H, 64, generator=g).to(torch.bfloat16)
+    q = x.permute(0, 2, 1, 3)                      # (B, H, L, D) view, row stride H*D
+    k = torch.randn(B, L, H, 64, generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)
+    v = torch.randn(B, L, H, 64, generator=g).to(torch.bfloat16).permute(0, 2, 1, 3)
+    full = torch.randn(32, 2 * H, generator=g).to(torch.bfloat16)
+    table = full[:, H:]                             # head slice, non-contiguous
+    op = _import_op()
+    dev = torch.device("cuda")
+    out = op(q.to(dev), k.to(dev), v.to(dev), table.to(dev), 32, 128, False, None, 0.0, 1.0)
+    ref = oracle.rpb_attention_ref(q.float(), k.float(), v.float(), table.float(), 32, 128, False, None, 1.0)
+    assert_close(out, ref, None, what="views")
+
+
+def test_rpb_golden_reference_case():
+    G = np.load(gi.__file__.replace("golden_inputs.py", "golden.npz"))
+    c = gi.t5_case("t5_enc")
+    op = _import_op()
+    dev = torch.device("cuda")
+    bf = torch.bfloat16
+    mask = c["mask"].to(bf)
+    out = op(c["q"].to(bf).to(dev), c["k"].to(bf).to(dev), c["v"].to(bf).to(dev), c["table"].to(bf).to(dev),
+             c["num_buckets"], c["max_distance"], False, mask.to(dev), 0.0, 1.0)
+    ref = torch.from_numpy(G["t5_enc_out"])
+    assert_close(out, ref, None, what="golden t5_enc")
+
+
+def test_rpb_c2_config_subset():
+    # BASELINE config C2 shape (B=16, L=768, H=16, D=64, 32 buckets / 128) with ragged
+    # lengths; the oracle checks two batch rows to bound CPU time.
+    from vf_b200.workloads import mt5_attention_inputs
+    w = mt5_attention_inputs(seed=0, device="cuda")
+    op = _import_op()
+    out = op(w["q"], w["k"], w["v"], w["rpb_table"], 32, 128, False, w["padding_mask"], 0.0, 1.0)
+    for b in (0, 9):
+        ref = oracle.rpb_attention_ref(w["q"][b:b + 1].float().cpu(), w["k"][b:b + 1].float().cpu(),
+                                       w["v"][b:b + 1].float().cpu(), w["rpb_table"].float().cpu(), 32, 128, False,
+                                       w["padding_mask"][b:b + 1].float().cpu(), 1.0)
+        valid = lens_mask(w["lengths"][b:b + 1], 768)
+        assert_close(out[b:b + 1], ref, valid, what=f"C2 batch {b} valid rows")
+        assert_close(out[b:b + 1], ref, None, what=f"C2 batch {b} all rows")
+
+
+def test_rpb_repeat_is_deterministic():
+    q, k, v, t, m = make_inputs(2, 2, 300, 300, torch.bfloat16, lens=[300, 200], seed=13)
+    op = _import_op()
+    dev = torch.device("cuda")
+    args = (q.to(dev), k.to(dev), v.to(dev), t.to(dev), 32, 128, False, m.to(dev), 0.0, 1.0)
+    a = op(*args)
+    b = op(*args)
+    assert torch.equal(a, b)
+    import vf_b200
+    assert vf_b200.device_error(clear=True) == 0
+
+
+def test_rpb_cpu_tensors_raise():
+    q, k, v, t, m = make_inputs(1, 1, 64, 64, torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        _import_op()(q, k, v, t, 32, 128, False, m)

@@ -1,0 +1,43 @@
+"""T5 relative-position-bias flash attention — drop-in for vllm-factory's
+kernels/flash_attention_rpb.py (`flash_attention_rpb_final`, :296-412).
+
+Computes, per (batch b, head h, query m):
+    s[n]   = softmax_scale * q[m]·k[n] + rpb_table[bucket(n - m), h] + padding_mask[b, h, m, n]
+    out[m] = softmax(s) @ v
+with the T5 bucket of models/mt5/mt5_encoder.py:125-148 (bidirectional unless
+`is_decoder`, which also applies a causal mask), clamped to the table's rows.
+The work runs in the sm_100a kernel of libvf_b200.so (tcgen05 UMMA, TMEM accumulators,
+TMA-staged K/V); there is no Triton and no CPU path.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+import vf_b200  # noqa: F401  (registers torch.ops.vf_b200)
+
+
+def flash_attention_rpb_final(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    rpb_table: Optional[torch.Tensor],
+    num_buckets: int,
+    max_distance: int,
+    is_decoder: bool,
+    padding_mask: Optional[torch.Tensor] = None,
+    dropout_p: float = 0.0,
+    softmax_scale: float = 1.0,
+    use_autotune: bool = True,
+) -> torch.Tensor:
+    """Same arguments and result as the reference.  `use_autotune` is accepted and ignored:
+    the kernel has a single tile configuration.  `dropout_p` must be 0 (inference path;
+    the reference's callers always pass 0)."""
+    del use_autotune
+    return torch.ops.vf_b200.rpb_attention(
+        q, k, v, rpb_table, int(num_buckets), int(max_distance), bool(is_decoder),
+        padding_mask, float(dropout_p), float(softmax_scale))
+
+
+__all__ = ["flash_attention_rpb_final"]

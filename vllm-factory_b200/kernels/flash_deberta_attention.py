@@ -1,0 +1,53 @@
+"""DeBERTa disentangled flash attention — drop-in for vllm-factory's
+kernels/flash_deberta_attention.py (`flash_deberta_attention`, :455-499).
+
+Computes, per (batch b, head h, query m < seq_len[b]):
+    idx    = clamp(bucket(m - n) + S, 0, 2S - 1)          S = position_buckets or max_rel
+    s[n]   = sm_scale * (q[m]·k[n] + pos_key[m, idx] + pos_query[n, idx]),  n < seq_len[b]
+    out[m] = softmax(s) @ v ;   rows m >= seq_len[b] are 0
+with bucket() the log bucket of models/deberta_v2/deberta_v2_encoder.py:70-89 when
+`use_log_bucket` (DeBERTa v2/v3) and the identity otherwise (DeBERTa v1).
+The work runs in the sm_100a kernel of libvf_b200.so; there is no Triton and no CPU path.
+
+`HAS_TRITON` keeps the reference's export name: the reference's encoders enable their
+fused path when it is true (models/deberta_v2/deberta_v2_encoder.py:39-40,
+models/deberta/deberta_encoder.py:35-36).  Here it means "the fused GPU op is present".
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+import vf_b200  # noqa: F401  (registers torch.ops.vf_b200)
+
+HAS_TRITON = True
+
+
+def flash_deberta_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    seq_lengths: Optional[torch.Tensor] = None,
+    pos_key: Optional[torch.Tensor] = None,
+    pos_query: Optional[torch.Tensor] = None,
+    causal: bool = False,
+    sm_scale: Optional[float] = None,
+    position_buckets: int = 0,
+    max_relative_distance: int = 0,
+    use_log_bucket: bool = False,
+) -> torch.Tensor:
+    """Same arguments and result as the reference (output rows past seq_len are zero)."""
+    return torch.ops.vf_b200.deberta_attention(
+        q, k, v, seq_lengths, pos_key, pos_query, bool(causal),
+        None if sm_scale is None else float(sm_scale),
+        int(position_buckets), int(max_relative_distance), bool(use_log_bucket))
+
+
+def clear_config_cache() -> None:
+    """Reference API (kernels/flash_deberta_attention.py:502).  The reference cached Triton
+    tile configurations; this implementation has a single configuration, so there is
+    nothing to clear."""
+
+
+__all__ = ["flash_deberta_attention", "clear_config_cache", "HAS_TRITON"]

@@ -1,0 +1,161 @@
+"""ctypes binding of libvf_b200.so (include/vf_b200.h).
+
+This is the binding a maintainer of the reference would add: the reference's Python
+launchers (kernels/flash_attention_rpb.py:296, kernels/flash_deberta_attention.py:455)
+called Triton; here they call the C entry points below.  Loading fails loudly: there is
+no CPU or Triton fallback behind this module.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("VF_B200_LIB", str(_PKG / "libvf_b200.so")))
+
+VF_OK = 0
+VF_EINVAL = -1
+VF_EUNSUPPORTED = -2
+VF_ECUDA = -3
+
+VF_DTYPE_F32 = 0
+VF_DTYPE_F16 = 1
+VF_DTYPE_BF16 = 2
+
+ABI_VERSION = 1
+
+EXPORTED_SYMBOLS = (
+    "vf_rpb_attention_fwd",
+    "vf_deberta_attention_fwd",
+    "vf_t5_relative_bucket",
+    "vf_deberta_log_bucket",
+    "vf_last_error",
+    "vf_device_error",
+    "vf_abi_version",
+)
+
+
+class Tensor4d(ctypes.Structure):
+    _fields_ = [
+        ("data", ctypes.c_void_p),
+        ("size", ctypes.c_int64 * 4),
+        ("stride", ctypes.c_int64 * 4),
+    ]
+
+
+class RpbArgs(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_int),
+        ("q", Tensor4d),
+        ("k", Tensor4d),
+        ("v", Tensor4d),
+        ("out", Tensor4d),
+        ("rpb_table", ctypes.c_void_p),
+        ("table_rows", ctypes.c_int64),
+        ("table_cols", ctypes.c_int64),
+        ("table_stride_row", ctypes.c_int64),
+        ("table_stride_col", ctypes.c_int64),
+        ("table_dtype", ctypes.c_int),
+        ("num_buckets", ctypes.c_int32),
+        ("max_distance", ctypes.c_int32),
+        ("is_decoder", ctypes.c_int32),
+        ("padding_mask", Tensor4d),
+        ("mask_dtype", ctypes.c_int),
+        ("dropout_p", ctypes.c_float),
+        ("softmax_scale", ctypes.c_float),
+    ]
+
+
+class DebertaArgs(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_int),
+        ("q", Tensor4d),
+        ("k", Tensor4d),
+        ("v", Tensor4d),
+        ("out", Tensor4d),
+        ("seq_lengths", ctypes.c_void_p),
+        ("pos_key", Tensor4d),
+        ("pos_query", Tensor4d),
+        ("causal", ctypes.c_int32),
+        ("has_sm_scale", ctypes.c_int32),
+        ("sm_scale", ctypes.c_float),
+        ("position_buckets", ctypes.c_int32),
+        ("max_relative_distance", ctypes.c_int32),
+        ("use_log_bucket", ctypes.c_int32),
+    ]
+
+
+class VfError(RuntimeError):
+    """A libvf_b200 entry point returned an error code."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"vf_b200 error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Loads the in-tree library once; raises if it is missing or has the wrong ABI."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} not found: build it with `python -m vf_b200.build` "
+                "(or __graft_entry__.build()); there is no fallback implementation")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        lib.vf_rpb_attention_fwd.argtypes = [ctypes.POINTER(RpbArgs), ctypes.c_void_p]
+        lib.vf_rpb_attention_fwd.restype = ctypes.c_int
+        lib.vf_deberta_attention_fwd.argtypes = [ctypes.POINTER(DebertaArgs), ctypes.c_void_p]
+        lib.vf_deberta_attention_fwd.restype = ctypes.c_int
+        lib.vf_t5_relative_bucket.argtypes = [ctypes.c_int32] * 5 + [ctypes.POINTER(ctypes.c_int32)]
+        lib.vf_t5_relative_bucket.restype = ctypes.c_int
+        lib.vf_deberta_log_bucket.argtypes = [ctypes.c_int32] * 4 + [ctypes.POINTER(ctypes.c_int32)]
+        lib.vf_deberta_log_bucket.restype = ctypes.c_int
+        lib.vf_last_error.argtypes = []
+        lib.vf_last_error.restype = ctypes.c_char_p
+        lib.vf_device_error.argtypes = [ctypes.c_int32]
+        lib.vf_device_error.restype = ctypes.c_int
+        lib.vf_abi_version.argtypes = []
+        lib.vf_abi_version.restype = ctypes.c_int
+        if lib.vf_abi_version() != ABI_VERSION:
+            raise RuntimeError(f"{LIB_PATH}: ABI version {lib.vf_abi_version()} != {ABI_VERSION}")
+        _lib = lib
+        return lib
+
+
+def check(rc: int) -> None:
+    if rc != VF_OK:
+        msg = load().vf_last_error().decode(errors="replace")
+        raise VfError(rc, msg)
+
+
+def t5_relative_bucket(num_buckets: int, max_distance: int, bidirectional: bool, rmin: int, rmax: int):
+    """Bucket of every relative position r in [rmin, rmax] (list of ints)."""
+    n = rmax - rmin + 1
+    buf = (ctypes.c_int32 * n)()
+    check(load().vf_t5_relative_bucket(num_buckets, max_distance, int(bidirectional), rmin, rmax, buf))
+    return list(buf)
+
+
+def deberta_log_bucket(bucket_size: int, max_position: int, rmin: int, rmax: int):
+    """DeBERTa log-bucket position of every relative position r in [rmin, rmax]."""
+    n = rmax - rmin + 1
+    buf = (ctypes.c_int32 * n)()
+    check(load().vf_deberta_log_bucket(bucket_size, max_position, rmin, rmax, buf))
+    return list(buf)
+
+
+def device_error(clear: bool = True) -> int:
+    rc = load().vf_device_error(int(clear))
+    if rc < 0:
+        check(rc)
+    return rc
