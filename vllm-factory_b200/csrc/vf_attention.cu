@@ -7,11 +7,14 @@
 //                s = sm_scale * (q.k + pos_key[m, idx(m - n)] + pos_query[n, idx(m - n)])
 //
 // CTA = 256 query rows of one (batch, head) as two 128-row tiles, keys in 128-row tiles.
-// Warp roles (320 threads):
+// Warp roles (384 threads = 3 warpgroups):
 //   warps 0-3  softmax group 0 (query tile 0), one thread per query row
 //   warps 4-7  softmax group 1 (query tile 1)
 //   warp  8    TMA producer (Q once, then a 3-stage K/V ring)
 //   warp  9    UMMA issuer (one elected lane) + TMEM allocation
+//   warps 10-11 idle
+// Launched at 168 registers/thread; after the prologue the producer warpgroup drops to
+// 40 and the softmax warpgroups rise to 232 (2*128*232 + 128*40 = 384*168).
 // TMEM (512 columns, fp32): per query tile g, S at 256g, P (bf16 pairs) at 256g+128,
 // O at 256g+192.  S = Q K^T and O += P V run on tcgen05.mma (kind::f16, fp32 accumulate);
 // softmax threads read S with tcgen05.ld, write P back with tcgen05.st, and the PV MMA
@@ -42,7 +45,9 @@ constexpr int kBN = 128;          // keys per tile
 constexpr int kHeadDim = 64;
 constexpr int kStages = 3;        // K/V ring depth
 constexpr int kTileBytes = kBM * kHeadDim * 2;   // 16 KB for a 128 x 64 16-bit tile
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+constexpr uint32_t kRegsSoftmax = 232;
+constexpr uint32_t kRegsProducer = 40;
 constexpr int kLoadWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
@@ -133,7 +138,7 @@ __device__ void zero_rows(const KParams& p, int b, int h, int r0, int r1, int ti
 }
 
 template <int kVariant, typename T>
-__global__ void __maxnreg__(200) attn_fwd_kernel(const __grid_constant__ KParams p) {
+__global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ KParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* kbias = reinterpret_cast<float*>(smem + kOffKBias);
@@ -232,6 +237,8 @@ __global__ void __maxnreg__(200) attn_fwd_kernel(const __grid_constant__ KParams
   }
   const int nkv = max(t_end - t_begin, 0);
 
+  if (warp >= 8) {
+  reg_dealloc<kRegsProducer>();
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && nkv > 0) {
@@ -239,6 +246,7 @@ __global__ void __maxnreg__(200) attn_fwd_kernel(const __grid_constant__ KParams
       for (int g = 0; g < kNQ; ++g)
         tma_load_4d(smem + kOffQ + g * kTileBytes, &p.tm_q, q_full, 0, q0 + g * kBM, h, b);
     }
+    int issued = 0;
     for (int t = 0; t < nkv; ++t) {
       const int s = t % kStages;
       const int round = t / kStages;
@@ -247,6 +255,7 @@ __global__ void __maxnreg__(200) attn_fwd_kernel(const __grid_constant__ KParams
         if (!__all_sync(0xffffffffu, ok)) break;
       }
       const int k0 = (t_begin + t) * kBN;
+      issued = t + 1;
       if (lane == 0) {
         mbar_arrive_expect_tx(&k_full[s], kTileBytes);
         tma_load_4d(smem + kOffK + s * kTileBytes, &p.tm_k, &k_full[s], 0, k0, h, b);
@@ -264,6 +273,15 @@ __global__ void __maxnreg__(200) attn_fwd_kernel(const __grid_constant__ KParams
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&k_full[s]);
+      }
+    }
+    // No TMA write may land after this CTA exits: wait for the last fills (already
+    // complete on the normal path), ignoring the abort flag but still time-bounded.
+    if (lane == 0 && nkv > 0) {
+      mbar_wait_bounded(q_full, 0);
+      for (int t = max(issued - kStages, 0); t < issued; ++t) {
+        mbar_wait_bounded(&k_full[t % kStages], (t / kStages) & 1);
+        mbar_wait_bounded(&v_full[t % kStages], (t / kStages) & 1);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -332,7 +350,17 @@ __global__ void __maxnreg__(200) attn_fwd_kernel(const __grid_constant__ KParams
       }
     }
     __syncwarp();
-  } else {
+    // TMEM is released once both softmax groups are done with it.
+    tc_fence_before();
+    named_bar_sync(1, 2 * 128 + 32);
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  return;
+  }
+
+  reg_alloc<kRegsSoftmax>();
+  {
     // ------------------------------------------------------------ softmax groups
     const int g = warp >> 2;                  // query tile
     const int row = (warp & 3) * 32 + lane;   // row inside the tile == TMEM lane
@@ -362,47 +390,46 @@ __global__ void __maxnreg__(200) attn_fwd_kernel(const __grid_constant__ KParams
       if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
       tc_fence_after();
 
-      uint32_t sr[kBN];
-      tmem_ld_x128(tS, sr);
+      // Scores in log2 units, 32 TMEM columns at a time (bounded register pressure; the
+      // asm's memory clobber also keeps each chunk's gathers behind its TMEM load).
       float x[kBN];
-      float mx = -INFINITY;
-      if (kVariant == kT5) {
-        const float* kb = kbias + (t % kStages) * kBN;
-        const int rb0 = k0 - m + R;   // index of r = n - m for column 0
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          const int ri = min(max(rb0 + c, 0), 2 * R);
-          float bias = rbias[ri];
-          if (has_mask) bias += kb[c];
-          x[c] = fmaf(__uint_as_float(sr[c]), scale_log2, bias);
-        }
-        if (k0 + kBN > p.N) {
+      for (int ch = 0; ch < kBN / 32; ++ch) {
+        uint32_t sr[32];
+        tmem_ld_x32(tS + 32 * ch, sr);
+        if (kVariant == kT5) {
+          const float* kb = kbias + (t % kStages) * kBN + 32 * ch;
+          const int rb0 = k0 + 32 * ch - m + R;   // index of r = n - m for this chunk's column 0
 #pragma unroll
-          for (int c = 0; c < kBN; ++c)
-            if (k0 + c >= p.N) x[c] = -INFINITY;
-        }
-        if (p.causal) {
+          for (int i = 0; i < 32; ++i) {
+            const int c = 32 * ch + i;
+            const int ri = min(max(rb0 + i, 0), 2 * R);
+            float bias = rbias[ri];
+            if (has_mask) bias += kb[i];
+            float xv = fmaf(__uint_as_float(sr[i]), scale_log2, bias);
+            if (k0 + c >= p.N || (p.causal && k0 + c > m)) xv = -INFINITY;
+            x[c] = xv;
+          }
+        } else {
 #pragma unroll
-          for (int c = 0; c < kBN; ++c)
-            if (k0 + c > m) x[c] = -INFINITY;
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          const int n = k0 + c;
-          float acc = __uint_as_float(sr[c]);
-          if (n < klen) {
-            const int r = min(max(m - n, -R), R);
-            const int idx = lut_s[r + R];
-            if (pk_row != nullptr) acc += to_f<T>(pk_row[idx * p.pk_sk]);
-            if (pq_base != nullptr) acc += to_f<T>(pq_base[(long long)n * p.pq_sn + idx * p.pq_sk]);
-            x[c] = acc * scale_log2;
-            if (p.causal && n > m + p.p_seq) x[c] = -INFINITY;
-          } else {
-            x[c] = -INFINITY;
+          for (int i = 0; i < 32; ++i) {
+            const int c = 32 * ch + i;
+            const int n = k0 + c;
+            float xv = -INFINITY;
+            if (n < klen) {
+              float acc = __uint_as_float(sr[i]);
+              const int r = min(max(m - n, -R), R);
+              const int idx = lut_s[r + R];
+              if (pk_row != nullptr) acc += to_f<T>(pk_row[idx * p.pk_sk]);
+              if (pq_base != nullptr) acc += to_f<T>(pq_base[(long long)n * p.pq_sn + idx * p.pq_sk]);
+              xv = acc * scale_log2;
+              if (p.causal && n > m + p.p_seq) xv = -INFINITY;
+            }
+            x[c] = xv;
           }
         }
       }
+      float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, x[c]);
 
@@ -438,45 +465,41 @@ __global__ void __maxnreg__(200) attn_fwd_kernel(const __grid_constant__ KParams
       mbar_arrive(&p_full[g]);
     }
 
-    // Epilogue: O / l, rows past the valid length written as zeros (DeBERTa).
-    if (m < p.M) {
-      T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * p.o_sh + (long long)m * p.o_sm;
-      uint32_t o[kHeadDim];
-      bool have = false;
-      if (nkv > 0 && !aborted) {
-        const bool ok = mbar_wait(o_full, 0, abort_flag);
-        if (__all_sync(0xffffffffu, ok)) {
-          tc_fence_after();
-          tmem_ld_x64(tO, o);
-          have = true;
-        }
-      }
-      const bool row_valid = (kVariant != kDeberta) || (m < qlen);
-      const float inv_l = (have && row_valid && l_run > 0.f) ? 1.f / l_run : 0.f;
-#pragma unroll
-      for (int i = 0; i < kHeadDim / 8; ++i) {
-        uint4 v;
-        v.x = pack2<T>(have ? __uint_as_float(o[8 * i + 0]) * inv_l : 0.f, have ? __uint_as_float(o[8 * i + 1]) * inv_l : 0.f);
-        v.y = pack2<T>(have ? __uint_as_float(o[8 * i + 2]) * inv_l : 0.f, have ? __uint_as_float(o[8 * i + 3]) * inv_l : 0.f);
-        v.z = pack2<T>(have ? __uint_as_float(o[8 * i + 4]) * inv_l : 0.f, have ? __uint_as_float(o[8 * i + 5]) * inv_l : 0.f);
-        v.w = pack2<T>(have ? __uint_as_float(o[8 * i + 6]) * inv_l : 0.f, have ? __uint_as_float(o[8 * i + 7]) * inv_l : 0.f);
-        *reinterpret_cast<uint4*>(orow + 8 * i) = v;
-      }
-    } else if (nkv > 0 && !aborted) {
-      // Rows past M still take part in the warp-collective TMEM load.
+    // Epilogue: O / l, rows past the valid length written as zeros (DeBERTa).  The wait
+    // and the TMEM load are warp-collective and run on every lane (`aborted` and `nkv` are
+    // warp-uniform); only the global store depends on the lane's row.
+    uint32_t o[kHeadDim];
+    bool have = false;
+    if (nkv > 0 && !aborted) {
       const bool ok = mbar_wait(o_full, 0, abort_flag);
       if (__all_sync(0xffffffffu, ok)) {
         tc_fence_after();
-        uint32_t o[kHeadDim];
         tmem_ld_x64(tO, o);
+        have = true;
+      }
+    }
+    if (m < p.M) {
+      T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * p.o_sh + (long long)m * p.o_sm;
+      const bool row_valid = (kVariant != kDeberta) || (m < qlen);
+      const bool use = have && row_valid && l_run > 0.f;
+      const float inv_l = use ? 1.f / l_run : 0.f;
+#pragma unroll
+      for (int i = 0; i < kHeadDim / 8; ++i) {
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = use ? __uint_as_float(o[8 * i + j]) * inv_l : 0.f;
+        uint4 v;
+        v.x = pack2<T>(f[0], f[1]);
+        v.y = pack2<T>(f[2], f[3]);
+        v.z = pack2<T>(f[4], f[5]);
+        v.w = pack2<T>(f[6], f[7]);
+        *reinterpret_cast<uint4*>(orow + 8 * i) = v;
       }
     }
   }
 
   tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+  named_bar_sync(1, 2 * 128 + 32);
 }
 
 }  // namespace vf
