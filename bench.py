@@ -1,0 +1,346 @@
+"""Benchmark of the relative-position attention hot path (one JSON line on rank 0).
+
+Default workload (the metric's own configuration): one mT5-large
+encoder self-attention layer with the T5 relative-position bias, bf16, 16 sequences x 768
+positions (valid lengths ~ U[256, 768], right padding), 16 heads x 64.  A "step" is one
+call of the drop-in `kernels.flash_attention_rpb.flash_attention_rpb_final` on that batch.
+
+  value        attention TFLOP/s over the whole job (valid work: 4*H*D*sum L_i^2), inputs
+               resident in HBM; each step reads a different input set (the rotation
+               spans > 3x the 126 MB L2), so no step is served from L2.
+  e2e          the same metric through the same public call with pinned HOST buffers:
+               every step copies q, k, v, table and mask host->device and the output
+               device->host inside the timed region.
+  roofline     dominant kernel vs the measured dense bf16 peak (MEASURED_PEAKS.json).
+  cpu_baseline the oracle (CPU restatement of the reference's torch path) on this host.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own 16-sequence shard
+(independent sequences, weak scaling); NCCL is used only for the barrier and to take the
+max time over ranks.  `--impl reference` times the reference's CPU implementation (the
+oracle port) on rank 0 and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "vllm-factory_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "RPB attention TFLOP/s (% bf16 peak); encoder tokens/s at 1/2/4/8 B200"
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return dict(bf16=d["bf16_tflops"], bf16_sustained=d["bf16_tflops_sustained"], hbm=d["hbm_gbs"],
+                    source="measured")
+    return dict(bf16=1590.0, bf16_sustained=1400.0, hbm=6650.0, source="fallback")
+
+
+def committed_traffic(workload: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get(workload)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workloads
+def build_workload(name: str, rank: int, device):
+    """Returns (list of input dicts, call(inputs) -> out, flops per step, tokens per step, config)."""
+    from vf_b200 import workloads as W
+
+    if name == "mt5_c2":
+        from kernels.flash_attention_rpb import flash_attention_rpb_final
+        base = W.mt5_attention_inputs(seed=1000 + rank, device=device)
+        lens = base["lengths"].tolist()
+        flops = W.core_flops(lens)
+
+        def call(x):
+            return flash_attention_rpb_final(x["q"], x["k"], x["v"], x["rpb_table"], 32, 128, False,
+                                             x["padding_mask"], 0.0, 1.0)
+
+        per_set = sum(base[k].numel() * base[k].element_size() for k in ("q", "k", "v")) * 4 // 3
+        cfg = {"workload": "C2 mT5-large encoder self-attention layer, T5 RPB 32 buckets/128",
+               "global_batch": 16, "seq_len": 768, "heads": 16, "head_dim": 64,
+               "lengths": "U[256,768] right-padded"}
+        keys = ("q", "k", "v", "rpb_table", "padding_mask")
+    elif name.startswith("deberta_c1") or name.startswith("deberta_c5"):
+        from kernels.flash_deberta_attention import flash_deberta_attention
+        if name == "deberta_c1":
+            base = W.deberta_attention_inputs(seed=2000 + rank, device=device)
+            cfg = {"workload": "C1 DeBERTa-v3-large disentangled layer (bf16 on GPU), c2p|p2c, 256 buckets",
+                   "global_batch": 8, "seq_len": 512, "lengths": "U[64,512] right-padded"}
+        else:
+            L = int(name.split("_")[-1])
+            base = W.deberta_attention_inputs(seed=3000 + rank, device=device, B=16384 // L, L=L,
+                                              lengths=[L] * (16384 // L))
+            cfg = {"workload": f"C5 DeBERTa long-context sweep, seq {L}", "global_batch": 16384 // L, "seq_len": L}
+        lens = base["lengths"].tolist()
+        flops = W.core_flops(lens) + W.deberta_pos_flops(lens)
+
+        def call(x):
+            return flash_deberta_attention(x["q"], x["k"], x["v"], x["seq_lengths"], x["pos_key"], x["pos_query"],
+                                           False, x["sm_scale"], 256, 512, True)
+
+        per_set = sum(base[k].numel() * base[k].element_size() for k in ("q", "k", "v", "pos_key", "pos_query"))
+        keys = ("q", "k", "v", "pos_key", "pos_query", "seq_lengths")
+        cfg.update({"heads": 16, "head_dim": 64, "mode": "compat (precomputed pos_key/pos_query)"})
+    else:
+        raise SystemExit(f"unknown workload {name}")
+
+    n_sets = max(1, math.ceil(3 * L2_BYTES / per_set))
+    sets = [base]
+    for _ in range(n_sets - 1):
+        sets.append({k: (v.clone() if isinstance(v, torch.Tensor) and v.is_cuda and k in keys else v)
+                     for k, v in base.items()})
+    cfg["l2"] = f"{n_sets} rotating input sets ({per_set / 2**20:.0f} MiB each) > 3x L2; no flush"
+    return sets, call, flops, float(sum(lens)), cfg, keys, lens
+
+
+def cpu_baseline(name: str, lens, budget_s: float = 12.0):
+    """Times the oracle (CPU restatement of the reference's torch path) on a bounded sample."""
+    import oracle
+    from vf_b200 import workloads as W
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    if name == "mt5_c2":
+        x = W.mt5_attention_inputs(seed=1000, device="cpu")
+        flops_done, t0, n = 0.0, time.perf_counter(), 0
+        while True:
+            b = n % x["q"].shape[0]
+            sl = slice(b, b + 1)
+            oracle.rpb_attention_ref(x["q"][sl].float(), x["k"][sl].float(), x["v"][sl].float(),
+                                     x["rpb_table"].float(), 32, 128, False, x["padding_mask"][sl].float(), 1.0,
+                                     dtype=torch.float32)
+            flops_done += W.core_flops([int(x["lengths"][b])])
+            n += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+        dt = time.perf_counter() - t0
+        sample = f"{n} sequences of the C2 batch, one at a time, fp32 torch on CPU (oracle port of the reference's SDPA path)"
+    else:
+        x = W.deberta_attention_inputs(seed=2000, device="cpu")
+        flops_done, t0, n = 0.0, time.perf_counter(), 0
+        while True:
+            b = n % x["q"].shape[0]
+            sl = slice(b, b + 1)
+            oracle.deberta_attention_ref(x["q"][sl].float(), x["k"][sl].float(), x["v"][sl].float(),
+                                         x["seq_lengths"][sl], x["pos_key"][sl].float(), x["pos_query"][sl].float(),
+                                         False, x["sm_scale"], 256, 512, True, dtype=torch.float32)
+            L = int(x["lengths"][b])
+            flops_done += W.core_flops([L]) + W.deberta_pos_flops([L])
+            n += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+        dt = time.perf_counter() - t0
+        sample = f"{n} sequences of the C1 batch, fp32 torch on CPU (oracle port of the reference's op fallback)"
+    return {"value": flops_done / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="mt5_c2")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cb = cpu_baseline(args.workload, None, budget_s=max(5.0, min(60.0, 2.0 * args.steps)))
+        line = {"metric": METRIC, "value": cb["value"], "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+                "warmup": warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic", "impl": "reference",
+                "config": {"workload": args.workload},
+                "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    import vf_b200
+    vf_b200.load()
+
+    sets, call, flops, tokens, cfg, keys, lens = build_workload(args.workload, rank, dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for i in range(warmup):
+        call(sets[i % len(sets)])
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        call(sets[i % len(sets)])
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+
+    t = torch.tensor([ms, flops, tokens], dtype=torch.float64, device=dev)
+    if world > 1:
+        tmax = t[:1].clone()
+        torch.distributed.all_reduce(tmax, op=torch.distributed.ReduceOp.MAX)
+        tsum = t[1:].clone()
+        torch.distributed.all_reduce(tsum, op=torch.distributed.ReduceOp.SUM)
+        ms_max, flops_all, tokens_all = tmax.item(), tsum[0].item(), tsum[1].item()
+    else:
+        ms_max, flops_all, tokens_all = ms, flops, tokens
+    value = flops_all * args.steps / (ms_max * 1e-3) / 1e12
+    ms_step = ms_max / args.steps
+
+    # ---- end to end through the public call, host buffers, copies inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        host = {k: (v.cpu().pin_memory() if isinstance(v, torch.Tensor) and v.is_cuda and k in keys else v)
+                for k, v in sets[0].items()}
+        h2d = sum(v.numel() * v.element_size() for k, v in host.items() if k in keys and isinstance(v, torch.Tensor))
+        out_host = torch.empty(sets[0]["q"].shape, dtype=sets[0]["q"].dtype).pin_memory()
+        d2h = out_host.numel() * out_host.element_size()
+
+        def e2e_step():
+            x = {k: (v.to(dev, non_blocking=True) if k in keys and isinstance(v, torch.Tensor) else v)
+                 for k, v in host.items()}
+            o = call(x)
+            out_host.copy_(o, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        n_e2e = max(3, min(args.steps, 30))
+        e0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ems = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(ems, op=torch.distributed.ReduceOp.MAX)
+        e2e = {"value": flops_all * n_e2e / (ems.item() * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": n_e2e}
+
+    if world > 1:
+        torch.distributed.barrier()
+    if rank != 0:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+
+    peaks = measured_peaks()
+    achieved = flops / (ms / args.steps * 1e-3) / 1e12      # this rank's launches
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16"], "traffic": committed_traffic(args.workload),
+                "peak_source": f"{peaks['source']} bf16 dense (burst)",
+                "algorithmic_flops_per_launch": flops}
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
+            "tokens_per_s": tokens_all * args.steps / (ms_max * 1e-3),
+            "pct_bf16_peak": value / (peaks["bf16"] * world),
+            "roofline": roofline, "gpu_launches": args.steps, "clocks": clocks, "e2e": e2e}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.workload, lens)
+    print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

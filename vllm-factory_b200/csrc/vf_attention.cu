@@ -14,7 +14,7 @@
 //   warp  9    UMMA issuer (one elected lane) + TMEM allocation
 //   warps 10-11 idle
 // Launched at 168 registers/thread; after the prologue the producer warpgroup drops to
-// 40 and the softmax warpgroups rise to 232 (2*128*232 + 128*40 = 384*168).
+// 56 and the softmax warpgroups rise to 224 (2*128*224 + 128*56 = 384*168).
 // TMEM (512 columns, fp32): per query tile g, S at 256g, P (bf16 pairs) at 256g+128,
 // O at 256g+192.  S = Q K^T and O += P V run on tcgen05.mma (kind::f16, fp32 accumulate);
 // softmax threads read S with tcgen05.ld, write P back with tcgen05.st, and the PV MMA
@@ -46,8 +46,8 @@ constexpr int kHeadDim = 64;
 constexpr int kStages = 3;        // K/V ring depth
 constexpr int kTileBytes = kBM * kHeadDim * 2;   // 16 KB for a 128 x 64 16-bit tile
 constexpr int kThreads = 384;
-constexpr uint32_t kRegsSoftmax = 232;
-constexpr uint32_t kRegsProducer = 40;
+constexpr uint32_t kRegsSoftmax = 224;
+constexpr uint32_t kRegsProducer = 56;
 constexpr int kLoadWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
@@ -90,9 +90,11 @@ struct __align__(64) KParams {
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kNQ * kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
+constexpr int kRPad = 160;                  // bias-table padding: a warp's window never clamps
 constexpr int kOffKBias = kOffV + kStages * kTileBytes;
-constexpr int kOffRBias = kOffKBias + kStages * kBN * 4;
-constexpr int kOffLut = kOffRBias + kMaxLut * 4 + 12;           // keep 16-byte alignment
+constexpr int kOffKZero = kOffKBias + kStages * kBN * 4;         // per stage: key mask all zero
+constexpr int kOffRBias = kOffKZero + 16;
+constexpr int kOffLut = kOffRBias + (kMaxLut + 2 * kRPad) * 4 + 12;   // keep 16-byte alignment
 constexpr int kOffBar = (kOffLut + kMaxLut * 2 + 15 + 64) & ~15;
 // barriers: q_full, s_full[2], p_full[2], o_full, k_full[3], v_full[3], kv_empty[3], drain
 constexpr int kNumBars = 1 + 2 + 2 + 1 + 3 * kStages + 1;
@@ -142,7 +144,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* kbias = reinterpret_cast<float*>(smem + kOffKBias);
-  float* rbias = reinterpret_cast<float*>(smem + kOffRBias);
+  float* rbias = reinterpret_cast<float*>(smem + kOffRBias);   // index r + R + kRPad
+  int* kzero = reinterpret_cast<int*>(smem + kOffKZero);
   short* lut_s = reinterpret_cast<short*>(smem + kOffLut);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars + 0;
@@ -202,13 +205,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     tma_prefetch_desc(&p.tm_v);
   }
   // Relative-position tables into shared memory.
-  for (int i = tid; i <= 2 * R; i += kThreads) {
-    const short v = p.lut[i];
-    lut_s[i] = v;
-    if (kVariant == kT5)
+  for (int i = tid; i <= 2 * R; i += kThreads) lut_s[i] = p.lut[i];
+  if (kVariant == kT5) {
+    // rbias[r + R + kRPad] = table[bucket(r), h] * log2(e) for r in [-R - kRPad, R + kRPad];
+    // beyond +-R the bucket is saturated, so the padding repeats the end values.
+    for (int i = tid; i <= 2 * (R + kRPad); i += kThreads) {
+      const int rc = min(max(i - kRPad, 0), 2 * R);
+      const short v = p.lut[rc];
       rbias[i] = (p.table != nullptr)
                      ? load_any(p.table, (long long)v * p.tb_srow + (long long)h * p.tb_scol, p.table_dtype) * kLog2e
                      : 0.f;
+    }
   }
   // T5: the span of keys whose mask is alive bounds the key tiles worth visiting.
   if (has_mask) {
@@ -263,14 +270,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         tma_load_4d(smem + kOffV + s * kTileBytes, &p.tm_v, &v_full[s], 0, k0, h, b);
       }
       if (has_mask) {
+        bool zero = true;
 #pragma unroll
         for (int i = 0; i < kBN / 32; ++i) {
           const int c = lane + 32 * i;
           const int n = k0 + c;
           float mv = 0.f;
           if (n < p.N) mv = load_any(p.mask, b * p.mk_sb + h * p.mk_sh + n * p.mk_sn, p.mask_dtype);
+          zero = zero && (mv == 0.f);
           kbias[s * kBN + c] = fmaxf(mv, kMaskFloor) * kLog2e;
         }
+        zero = __all_sync(0xffffffffu, zero);
+        if (lane == 0) kzero[s] = zero ? 1 : 0;
         __syncwarp();
         if (lane == 0) mbar_arrive(&k_full[s]);
       }
@@ -390,27 +401,56 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
       tc_fence_after();
 
-      // Scores in log2 units, 32 TMEM columns at a time (bounded register pressure; the
-      // asm's memory clobber also keeps each chunk's gathers behind its TMEM load).
-      float x[kBN];
+      // Scores in log2 units.  TMEM is read 32 columns at a time (bounded register
+      // pressure; the asm's memory clobber also keeps each chunk's loads behind its TMEM
+      // load).  x2[j] holds columns 2j, 2j+1.
+      float2 x2[kBN / 2];
+      if constexpr (kVariant == kT5) {
+        // Warp-uniform tile class over the warp's 32 rows: r = n - m in [r_lo, r_hi].
+        const int m0 = m - lane;
+        const int r_lo = k0 - (m0 + 31);
+        const int r_hi = k0 + kBN - 1 - m0;
+        const float2 sc2 = make_float2(scale_log2, scale_log2);
+        const bool saturated = (r_lo >= R) || (r_hi <= -R);
+        tmem_ld_x128_f2(tS, x2);
+        // The key mask (additive, per key) joins the bias operand of the single FMA pass;
+        // tiles whose mask is all zero skip it.
+        const bool kadd = has_mask && !kzero[t % kStages];
+        const float2* kb2 = reinterpret_cast<const float2*>(kbias + (t % kStages) * kBN);
+        if (saturated) {
+          const float cb = rbias[(r_lo >= R ? 2 * R : 0) + kRPad];
+          const float2 cb2 = make_float2(cb, cb);
+          if (kadd) {
 #pragma unroll
-      for (int ch = 0; ch < kBN / 32; ++ch) {
-        uint32_t sr[32];
-        tmem_ld_x32(tS + 32 * ch, sr);
-        if (kVariant == kT5) {
-          const float* kb = kbias + (t % kStages) * kBN + 32 * ch;
-          const int rb0 = k0 + 32 * ch - m + R;   // index of r = n - m for this chunk's column 0
+            for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(cb2, kb2[j]));
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = 32 * ch + i;
-            const int ri = min(max(rb0 + i, 0), 2 * R);
-            float bias = rbias[ri];
-            if (has_mask) bias += kb[i];
-            float xv = fmaf(__uint_as_float(sr[i]), scale_log2, bias);
-            if (k0 + c >= p.N || (p.causal && k0 + c > m)) xv = -INFINITY;
-            x[c] = xv;
+            for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, cb2);
           }
         } else {
+          const float* rb = rbias + (k0 - m + R + kRPad);   // rb[c] = bias of column c
+          if (kadd) {
+#pragma unroll
+            for (int j = 0; j < kBN / 2; ++j)
+              x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(make_float2(rb[2 * j], rb[2 * j + 1]), kb2[j]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, make_float2(rb[2 * j], rb[2 * j + 1]));
+          }
+        }
+        if (k0 + kBN > p.N || (p.causal && r_hi > 0)) {
+#pragma unroll
+          for (int j = 0; j < kBN / 2; ++j) {
+            const int n = k0 + 2 * j;
+            if (n >= p.N || (p.causal && n > m)) x2[j].x = -INFINITY;
+            if (n + 1 >= p.N || (p.causal && n + 1 > m)) x2[j].y = -INFINITY;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int ch = 0; ch < kBN / 32; ++ch) {
+          uint32_t sr[32];
+          tmem_ld_x32(tS + 32 * ch, sr);
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int c = 32 * ch + i;
@@ -425,13 +465,23 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
               xv = acc * scale_log2;
               if (p.causal && n > m + p.p_seq) xv = -INFINITY;
             }
-            x[c] = xv;
+            if (i & 1) x2[c >> 1].y = xv; else x2[c >> 1].x = xv;
           }
         }
       }
-      float mx = -INFINITY;
+      // Row max: four independent 3-input max chains.
+      float mx;
+      {
+        float a[4];
 #pragma unroll
-      for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, x[c]);
+        for (int i = 0; i < 4; ++i) a[i] = fmaxf(x2[i].x, x2[i].y);
+#pragma unroll
+        for (int j = 4; j < kBN / 2; j += 4) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a[i] = fmax3(a[i], x2[j + i].x, x2[j + i].y);
+        }
+        mx = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3]));
+      }
 
       // Online softmax with lazy rescaling: the running max only moves (and O, l are
       // rescaled) when a row's max grows by more than kRescaleThreshold.
@@ -440,26 +490,31 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       if (__any_sync(0xffffffffu, need)) {
         const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
         if (t > 0) {
-          uint32_t o[kHeadDim];
-          tmem_ld_x64(tO, o);
 #pragma unroll
-          for (int i = 0; i < kHeadDim; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st_x64(tO, o);
+          for (int ch = 0; ch < kHeadDim / 16; ++ch) {
+            uint32_t o[16];
+            tmem_ld_x16(tO + 16 * ch, o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_x16(tO + 16 * ch, o);
+          }
         }
         l_run *= alpha;
         if (need) m_run = m_new;
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      const float2 neg_m2 = make_float2(-m_use, -m_use);
       uint32_t pk[kBN / 2];
-      float lsum = 0.f;
+      float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < kBN / 2; ++i) {
-        const float p0 = ex2_approx(x[2 * i] - m_use);
-        const float p1 = ex2_approx(x[2 * i + 1] - m_use);
-        lsum += p0 + p1;
-        pk[i] = pack2<T>(p0, p1);
+      for (int j = 0; j < kBN / 2; ++j) {
+        const float2 y = __fadd2_rn(x2[j], neg_m2);
+        const float2 e = make_float2(ex2_approx(y.x), ex2_approx(y.y));
+        if (j & 1) ls1 = __fadd2_rn(ls1, e); else ls0 = __fadd2_rn(ls0, e);
+        pk[j] = pack2<T>(e.x, e.y);
       }
-      l_run += lsum;
+      const float2 ls = __fadd2_rn(ls0, ls1);
+      l_run += ls.x + ls.y;
       tmem_st_x64(tP, pk);
       tc_fence_before();
       mbar_arrive(&p_full[g]);

@@ -215,11 +215,26 @@ __device__ __forceinline__ void tmem_st_x64(uint32_t taddr, const uint32_t (&r)[
                :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "r"(r[32]), "r"(r[33]), "r"(r[34]), "r"(r[35]), "r"(r[36]), "r"(r[37]), "r"(r[38]), "r"(r[39]), "r"(r[40]), "r"(r[41]), "r"(r[42]), "r"(r[43]), "r"(r[44]), "r"(r[45]), "r"(r[46]), "r"(r[47]), "r"(r[48]), "r"(r[49]), "r"(r[50]), "r"(r[51]), "r"(r[52]), "r"(r[53]), "r"(r[54]), "r"(r[55]), "r"(r[56]), "r"(r[57]), "r"(r[58]), "r"(r[59]), "r"(r[60]), "r"(r[61]), "r"(r[62]), "r"(r[63]) : "memory");
 }
 
+// Loads 128 consecutive fp32 columns of this thread's TMEM lane into x[64] (pairs) and
+// waits for them, in one asm statement.
+__device__ __forceinline__ void tmem_ld_x128_f2(uint32_t taddr, float2 (&x)[64]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];\n"
+               "tcgen05.wait::ld.sync.aligned;\n"
+               : "=f"(x[0].x), "=f"(x[0].y), "=f"(x[1].x), "=f"(x[1].y), "=f"(x[2].x), "=f"(x[2].y), "=f"(x[3].x), "=f"(x[3].y), "=f"(x[4].x), "=f"(x[4].y), "=f"(x[5].x), "=f"(x[5].y), "=f"(x[6].x), "=f"(x[6].y), "=f"(x[7].x), "=f"(x[7].y), "=f"(x[8].x), "=f"(x[8].y), "=f"(x[9].x), "=f"(x[9].y), "=f"(x[10].x), "=f"(x[10].y), "=f"(x[11].x), "=f"(x[11].y), "=f"(x[12].x), "=f"(x[12].y), "=f"(x[13].x), "=f"(x[13].y), "=f"(x[14].x), "=f"(x[14].y), "=f"(x[15].x), "=f"(x[15].y), "=f"(x[16].x), "=f"(x[16].y), "=f"(x[17].x), "=f"(x[17].y), "=f"(x[18].x), "=f"(x[18].y), "=f"(x[19].x), "=f"(x[19].y), "=f"(x[20].x), "=f"(x[20].y), "=f"(x[21].x), "=f"(x[21].y), "=f"(x[22].x), "=f"(x[22].y), "=f"(x[23].x), "=f"(x[23].y), "=f"(x[24].x), "=f"(x[24].y), "=f"(x[25].x), "=f"(x[25].y), "=f"(x[26].x), "=f"(x[26].y), "=f"(x[27].x), "=f"(x[27].y), "=f"(x[28].x), "=f"(x[28].y), "=f"(x[29].x), "=f"(x[29].y), "=f"(x[30].x), "=f"(x[30].y), "=f"(x[31].x), "=f"(x[31].y), "=f"(x[32].x), "=f"(x[32].y), "=f"(x[33].x), "=f"(x[33].y), "=f"(x[34].x), "=f"(x[34].y), "=f"(x[35].x), "=f"(x[35].y), "=f"(x[36].x), "=f"(x[36].y), "=f"(x[37].x), "=f"(x[37].y), "=f"(x[38].x), "=f"(x[38].y), "=f"(x[39].x), "=f"(x[39].y), "=f"(x[40].x), "=f"(x[40].y), "=f"(x[41].x), "=f"(x[41].y), "=f"(x[42].x), "=f"(x[42].y), "=f"(x[43].x), "=f"(x[43].y), "=f"(x[44].x), "=f"(x[44].y), "=f"(x[45].x), "=f"(x[45].y), "=f"(x[46].x), "=f"(x[46].y), "=f"(x[47].x), "=f"(x[47].y), "=f"(x[48].x), "=f"(x[48].y), "=f"(x[49].x), "=f"(x[49].y), "=f"(x[50].x), "=f"(x[50].y), "=f"(x[51].x), "=f"(x[51].y), "=f"(x[52].x), "=f"(x[52].y), "=f"(x[53].x), "=f"(x[53].y), "=f"(x[54].x), "=f"(x[54].y), "=f"(x[55].x), "=f"(x[55].y), "=f"(x[56].x), "=f"(x[56].y), "=f"(x[57].x), "=f"(x[57].y), "=f"(x[58].x), "=f"(x[58].y), "=f"(x[59].x), "=f"(x[59].y), "=f"(x[60].x), "=f"(x[60].y), "=f"(x[61].x), "=f"(x[61].y), "=f"(x[62].x), "=f"(x[62].y), "=f"(x[63].x), "=f"(x[63].y)
+               : "r"(taddr) : "memory");
+}
+
 // ---------------------------------------------------------------- math helpers
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
