@@ -1,0 +1,941 @@
+// sm_100a forward attention with additive relative-position terms.
+//
+// One kernel template serves both reference operators:
+//   * kT5      — kernels/flash_attention_rpb.py:62-230 (_flash_attn_rpb_fwd_kernel_final):
+//                s = scale * q.k + rpb_table[bucket(n - m), h] + padding_mask[b, h, n]
+//   * kDeberta — kernels/flash_deberta_attention.py:145-299 (_flash_deberta_fwd_kernel):
+//                s = sm_scale * (q.k + pos_key[m, idx(m - n)] + pos_query[n, idx(m - n)])
+//
+// CTA = 256 query rows of one (batch, head) as two 128-row tiles, keys in 128-row tiles.
+// Warp roles (384 threads = 3 warpgroups):
+//   warps 0-3  softmax group 0 (query tile 0), one thread per query row
+//   warps 4-7  softmax group 1 (query tile 1)
+//   warp  8    TMA producer (Q once, then a 3-stage K/V ring)
+//   warp  9    UMMA issuer (one elected lane) + TMEM allocation
+//   warps 10-11 idle
+// Launched at 168 registers/thread; after the prologue the producer warpgroup drops to
+// 56 and the softmax warpgroups rise to 224 (2*128*224 + 128*56 = 384*168).
+// TMEM (512 columns, fp32): per query tile g, S at 256g, P (bf16 pairs) at 256g+128,
+// O at 256g+192.  S = Q K^T and O += P V run on tcgen05.mma (kind::f16, fp32 accumulate);
+// softmax threads read S with tcgen05.ld, write P back with tcgen05.st, and the PV MMA
+// takes P straight from TMEM.  All waits are bounded (see vf_ptx.cuh).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "vf_ptx.cuh"
+#include "/root/repo/include/vf_b200.h"
+
+namespace vf {
+__device__ long long g_trace[4096];
+#define TR(slot) do { if (blockIdx.x == 1 && blockIdx.y == 0 && blockIdx.z == 0) g_trace[(slot)] = clock64(); } while (0)
+
+constexpr int kBM = 128;          // query rows per tile
+constexpr int kNQ = 2;            // query tiles per CTA
+constexpr int kBN = 128;          // keys per tile
+constexpr int kHeadDim = 64;
+constexpr int kStages = 3;        // K/V ring depth
+constexpr int kTileBytes = kBM * kHeadDim * 2;   // 16 KB for a 128 x 64 16-bit tile
+constexpr int kThreads = 384;
+constexpr uint32_t kRegsSoftmax = 224;
+constexpr uint32_t kRegsProducer = 56;
+constexpr int kLoadWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kMaxRel = 2048;               // relative-position table radius limit
+constexpr int kMaxLut = 2 * kMaxRel + 1;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kDeadMask = -1.0e4f;        // additive mask at/below this kills a key
+constexpr float kMaskFloor = -1.0e30f;      // masks are clamped here before scaling
+constexpr float kRescaleThreshold = 8.0f;   // lazy O rescale (log2 units)
+constexpr int kPolyEvery = 3;               // every 3rd exponential pair on the FMA pipe
+
+enum Variant : int { kT5 = 0, kDeberta = 1 };
+
+struct __align__(64) KParams {
+  CUtensorMap tm_q, tm_k, tm_v;
+  void* out;
+  long long o_sb, o_sh, o_sm;
+  int B, H, M, N;
+  float scale_log2;      // softmax scale * log2(e)
+  int causal;
+  int rel_R;             // lut covers relative positions [-rel_R, rel_R]
+  // T5 bias
+  const void* table;
+  long long tb_srow, tb_scol;
+  int table_dtype;
+  const void* mask;
+  long long mk_sb, mk_sh, mk_sn;
+  int mask_dtype;
+  // DeBERTa positions
+  const void* pos_key;
+  long long pk_sb, pk_sh, pk_sm, pk_sk;
+  const void* pos_query;
+  long long pq_sb, pq_sh, pq_sn, pq_sk;
+  const int* seq_lengths;
+  int p_seq;             // N - M (causal offset)
+  int span2;             // 2 * ATT_SPAN, bound of the position index
+  short lut[kMaxLut];    // T5: bucket of r = n - m;  DeBERTa: idx of r = m - n
+};
+
+// Shared-memory carve-up (offsets from a 1024-aligned base).
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kNQ * kTileBytes;
+constexpr int kOffV = kOffK + kStages * kTileBytes;
+constexpr int kRPad = 160;                  // bias-table padding: a warp's window never clamps
+constexpr int kOffKBias = kOffV + kStages * kTileBytes;
+constexpr int kOffKZero = kOffKBias + kStages * kBN * 4;         // per stage: key mask all zero
+constexpr int kOffRBias = kOffKZero + 16;
+constexpr int kOffLut = kOffRBias + (kMaxLut + 2 * kRPad) * 4 + 12;   // keep 16-byte alignment
+constexpr int kOffBar = (kOffLut + kMaxLut * 2 + 15 + 64) & ~15;
+// barriers: q_full, s_full[2], p_full[2], s_consumed[2], pv_done[2], k_full[3], v_full[3],
+// kv_empty[3], drain
+constexpr int kNumBars = 1 + 2 + 2 + 2 + 2 + 3 * kStages + 1;
+constexpr int kOffMisc = kOffBar + kNumBars * 8;
+constexpr int kSmemBytes = kOffMisc + 64;
+constexpr int kSmemAlloc = kSmemBytes + 1024;
+
+struct SmemMisc {
+  uint32_t tmem_base;
+  int abort_flag;
+  int live_lo;
+  int live_hi;
+};
+
+template <typename T> __device__ __forceinline__ float to_f(T v);
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> __device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+
+__device__ __forceinline__ float load_any(const void* p, long long off, int dtype) {
+  if (dtype == VF_DTYPE_F32) return __ldg(reinterpret_cast<const float*>(p) + off);
+  if (dtype == VF_DTYPE_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[off]);
+  return __half2float(reinterpret_cast<const __half*>(p)[off]);
+}
+
+template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) { return pack_bf16x2(lo, hi); }
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) { return pack_f16x2(lo, hi); }
+
+template <typename T> struct AbFormat;
+template <> struct AbFormat<__nv_bfloat16> { static constexpr uint32_t value = 1u; };
+template <> struct AbFormat<__half> { static constexpr uint32_t value = 0u; };
+
+// Writes zeros to output rows [r0, r1) of (b, h); used for DeBERTa rows past seq_len.
+template <typename T>
+__device__ void zero_rows(const KParams& p, int b, int h, int r0, int r1, int tid, int nthr) {
+  T* out = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * p.o_sh;
+  const int chunks = (r1 - r0) * (kHeadDim / 8);
+  for (int i = tid; i < chunks; i += nthr) {
+    const int r = r0 + i / (kHeadDim / 8);
+    const int c = (i % (kHeadDim / 8)) * 8;
+    *reinterpret_cast<uint4*>(out + r * p.o_sm + c) = make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <int kVariant, typename T>
+__global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ KParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* kbias = reinterpret_cast<float*>(smem + kOffKBias);
+  float* rbias = reinterpret_cast<float*>(smem + kOffRBias);   // index r + R + kRPad
+  int* kzero = reinterpret_cast<int*>(smem + kOffKZero);
+  short* lut_s = reinterpret_cast<short*>(smem + kOffLut);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* s_full = bars + 1;        // [2] S = Q K^T of the tile is in TMEM
+  uint64_t* p_full = bars + 3;        // [2] P of the tile is in TMEM
+  uint64_t* s_consumed = bars + 5;    // [2] softmax has read S into registers
+  uint64_t* pv_done = bars + 7;       // [2] O += P V of the tile has completed
+  uint64_t* k_full = bars + 9;        // [kStages]
+  uint64_t* v_full = k_full + kStages;
+  uint64_t* kv_empty = v_full + kStages;
+  uint64_t* drain = kv_empty + kStages;
+  SmemMisc* misc = reinterpret_cast<SmemMisc*>(smem + kOffMisc);
+  volatile int* abort_flag = &misc->abort_flag;
+
+  if (threadIdx.x == 0) TR(0);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int q0 = blockIdx.x * (kNQ * kBM);
+  const int R = p.rel_R;
+
+  // Valid keys / rows.  DeBERTa: seq_lengths (right padding); rows past it are written 0.
+  int klen = p.N, qlen = p.M;
+  if (kVariant == kDeberta && p.seq_lengths != nullptr) {
+    const int L = p.seq_lengths[b];
+    klen = min(max(L, 0), p.N);
+    qlen = min(max(L, 0), p.M);
+  }
+  if (kVariant == kDeberta && q0 >= qlen) {
+    zero_rows<T>(p, b, h, q0, min(q0 + kNQ * kBM, p.M), tid, kThreads);
+    return;
+  }
+
+  const bool has_mask = (kVariant == kT5) && (p.mask != nullptr);
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int g = 0; g < kNQ; ++g) {
+      mbar_init(&s_full[g], 1);
+      mbar_init(&p_full[g], kBM);
+      mbar_init(&s_consumed[g], kBM);
+      mbar_init(&pv_done[g], 1);
+    }
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&k_full[s], has_mask ? 2 : 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(drain, 1);
+    misc->abort_flag = 0;
+    misc->live_lo = 0x7fffffff;
+    misc->live_hi = -1;
+    fence_mbar_init();
+    // Q does not depend on the key range: start its copy before the prologue work.
+    mbar_arrive_expect_tx(q_full, kNQ * kTileBytes);
+    for (int g = 0; g < kNQ; ++g)
+      tma_load_4d(smem + kOffQ + g * kTileBytes, &p.tm_q, q_full, 0, q0 + g * kBM, h, b);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc(&misc->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == kLoadWarp && lane == 0) {
+    tma_prefetch_desc(&p.tm_q);
+    tma_prefetch_desc(&p.tm_k);
+    tma_prefetch_desc(&p.tm_v);
+  }
+  // Relative-position tables into shared memory.
+  for (int i = tid; i <= 2 * R; i += kThreads) lut_s[i] = p.lut[i];
+  if (kVariant == kT5) {
+    // rbias[r + R + kRPad] = table[bucket(r), h] * log2(e) for r in [-R - kRPad, R + kRPad];
+    // beyond +-R the bucket is saturated, so the padding repeats the end values.
+    for (int i = tid; i <= 2 * (R + kRPad); i += kThreads) {
+      const int rc = min(max(i - kRPad, 0), 2 * R);
+      const short v = p.lut[rc];
+      rbias[i] = (p.table != nullptr)
+                     ? load_any(p.table, (long long)v * p.tb_srow + (long long)h * p.tb_scol, p.table_dtype) * kLog2e
+                     : 0.f;
+    }
+  }
+  // T5: the span of keys whose mask is alive bounds the key tiles worth visiting.
+  if (has_mask) {
+    int lo = 0x7fffffff, hi = -1;
+    for (int n = tid; n < p.N; n += kThreads) {
+      const float mv = load_any(p.mask, b * p.mk_sb + h * p.mk_sh + n * p.mk_sn, p.mask_dtype);
+      if (mv > kDeadMask) { lo = min(lo, n); hi = max(hi, n); }
+    }
+    if (hi >= 0) { atomicMin(&misc->live_lo, lo); atomicMax(&misc->live_hi, hi); }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) TR(1);
+  const uint32_t tmem = misc->tmem_base;
+
+  // Key-tile range [t_begin, t_end).
+  int t_begin = 0, t_end = (klen + kBN - 1) / kBN;
+  if (has_mask && misc->live_hi >= 0) {
+    t_begin = misc->live_lo / kBN;
+    t_end = misc->live_hi / kBN + 1;
+  }
+  if (p.causal) {
+    // Keys a row may see: n <= m + p_seq, m < q0 + 256.
+    const int last_key = min(q0 + kNQ * kBM, p.M) - 1 + p.p_seq;
+    t_end = min(t_end, last_key < 0 ? 0 : last_key / kBN + 1);
+  }
+  const int nkv = max(t_end - t_begin, 0);
+
+  if (warp >= 8) {
+  reg_dealloc<kRegsProducer>();
+  if (warp == kLoadWarp) {
+    // ------------------------------------------------------------ TMA producer
+    int issued = 0;
+    for (int t = 0; t < nkv; ++t) {
+      const int s = t % kStages;
+      const int round = t / kStages;
+      if (round > 0) {
+        const bool ok = mbar_wait(&kv_empty[s], (round - 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) break;
+      }
+      const int k0 = (t_begin + t) * kBN;
+      issued = t + 1;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+        tma_load_4d(smem + kOffK + s * kTileBytes, &p.tm_k, &k_full[s], 0, k0, h, b);
+        mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+        tma_load_4d(smem + kOffV + s * kTileBytes, &p.tm_v, &v_full[s], 0, k0, h, b);
+      }
+      if (has_mask) {
+        bool zero = true;
+#pragma unroll
+        for (int i = 0; i < kBN / 32; ++i) {
+          const int c = lane + 32 * i;
+          const int n = k0 + c;
+          float mv = 0.f;
+          if (n < p.N) mv = load_any(p.mask, b * p.mk_sb + h * p.mk_sh + n * p.mk_sn, p.mask_dtype);
+          zero = zero && (mv == 0.f);
+          kbias[s * kBN + c] = fmaxf(mv, kMaskFloor) * kLog2e;
+        }
+        zero = __all_sync(0xffffffffu, zero);
+        if (lane == 0) kzero[s] = zero ? 1 : 0;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&k_full[s]);
+      }
+    }
+    // No TMA write may land after this CTA exits: wait for the last fills (already
+    // complete on the normal path), ignoring the abort flag but still time-bounded.
+    if (lane == 0) {
+      mbar_wait_bounded(q_full, 0);
+      for (int t = max(issued - kStages, 0); t < issued; ++t) {
+        mbar_wait_bounded(&k_full[t % kStages], (t / kStages) & 1);
+        mbar_wait_bounded(&v_full[t % kStages], (t / kStages) & 1);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (lane == 0 && nkv > 0) {
+      constexpr uint32_t fmt = AbFormat<T>::value;
+      constexpr uint32_t idesc_qk = idesc_f16(fmt, kBM, kBN, 0, 0);
+      constexpr uint32_t idesc_pv = idesc_f16(fmt, kBM, kHeadDim, 0, 1);
+      const uint32_t sQ = smem_u32(smem + kOffQ);
+      const uint32_t sK = smem_u32(smem + kOffK);
+      const uint32_t sV = smem_u32(smem + kOffV);
+      auto issue_qk = [&](int g, int s) {
+#pragma unroll
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+          const uint64_t ad = smem_desc_sw128(sQ + g * kTileBytes + kk * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(sK + s * kTileBytes + kk * 32, 16, 1024);
+          umma_ss(tmem + 256 * g, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int g, int s, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t bd = smem_desc_sw128(sV + s * kTileBytes + kk * 2048, 0, 1024);
+          umma_ts(tmem + 256 * g + 192, tmem + 256 * g + 128 + kk * 8, bd, idesc_pv,
+                  (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      // Order per key tile t: as soon as a group has read S(t) into registers, its
+      // S(t+1) = Q K(t+1)^T is issued (it overlaps that group's exponentials); PV(t) is
+      // issued when the group's P(t) is in TMEM.
+      bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
+      TR(2);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        umma_commit(&s_full[0]);
+        issue_qk(1, 0);
+        umma_commit(&s_full[1]);
+        for (int t = 0; t < nkv; ++t) {
+          const int s = t % kStages;
+          const bool has_next = t + 1 < nkv;
+          const int s2 = (t + 1) % kStages;
+          if (has_next && !mbar_wait(&k_full[s2], ((t + 1) / kStages) & 1, abort_flag)) break;
+          if (!mbar_wait(&s_consumed[0], t & 1, abort_flag)) break;
+          if (has_next) {
+            tc_fence_after();
+            issue_qk(0, s2);
+            umma_commit(&s_full[0]);
+          }
+          if (!mbar_wait(&s_consumed[1], t & 1, abort_flag)) break;
+          if (has_next) {
+            tc_fence_after();
+            issue_qk(1, s2);
+            umma_commit(&s_full[1]);
+          }
+          if (!mbar_wait(&v_full[s], (t / kStages) & 1, abort_flag)) break;
+          if (!mbar_wait(&p_full[0], t & 1, abort_flag)) break;
+          TR(100 + 8 * t + 0);
+          tc_fence_after();
+          issue_pv(0, s, t > 0);
+          umma_commit(&pv_done[0]);
+          if (!mbar_wait(&p_full[1], t & 1, abort_flag)) break;
+          TR(100 + 8 * t + 1);
+          tc_fence_after();
+          issue_pv(1, s, t > 0);
+          umma_commit(&pv_done[1]);
+          umma_commit(&kv_empty[s]);
+        }
+      }
+      // Drain: every MMA issued above has completed before TMEM is released.
+      umma_commit(drain);
+      {
+        const uint32_t a = smem_u32(drain);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(a, 0) && clock64() - t0 < kWaitCycles) {}
+      }
+    }
+    __syncwarp();
+    // TMEM is released once both softmax groups are done with it.
+    tc_fence_before();
+    named_bar_sync(1, 2 * 128 + 32);
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  return;
+  }
+
+  reg_alloc<kRegsSoftmax>();
+  {
+    // ------------------------------------------------------------ softmax groups
+    const int g = warp >> 2;                  // query tile
+    const int row = (warp & 3) * 32 + lane;   // row inside the tile == TMEM lane
+    const int m = q0 + g * kBM + row;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off + 256 * g;
+    const uint32_t tP = tS + 128;
+    const uint32_t tO = tS + 192;
+    const float scale_log2 = p.scale_log2;
+
+    const T* pk_row = nullptr;
+    const T* pq_base = nullptr;
+    if (kVariant == kDeberta) {
+      if (p.pos_key != nullptr && m < p.M)
+        pk_row = reinterpret_cast<const T*>(p.pos_key) + b * p.pk_sb + h * p.pk_sh + (long long)m * p.pk_sm;
+      if (p.pos_query != nullptr)
+        pq_base = reinterpret_cast<const T*>(p.pos_query) + b * p.pq_sb + h * p.pq_sh;
+    }
+
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool aborted = false;
+    for (int t = 0; t < nkv; ++t) {
+      const int k0 = (t_begin + t) * kBN;
+      bool ok = mbar_wait(&s_full[g], t & 1, abort_flag);
+      if (has_mask) ok = ok && mbar_wait(&k_full[t % kStages], (t / kStages) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+      if (row == 0) TR(200 + 16 * t + 8 * g + 0);
+      tc_fence_after();
+
+      // Scores in log2 units.  TMEM is read 32 columns at a time (bounded register
+      // pressure; the asm's memory clobber also keeps each chunk's loads behind its TMEM
+      // load).  x2[j] holds columns 2j, 2j+1.
+      float2 x2[kBN / 2];
+      if constexpr (kVariant == kT5) {
+        // Warp-uniform tile class over the warp's 32 rows: r = n - m in [r_lo, r_hi].
+        const int m0 = m - lane;
+        const int r_lo = k0 - (m0 + 31);
+        const int r_hi = k0 + kBN - 1 - m0;
+        const float2 sc2 = make_float2(scale_log2, scale_log2);
+        const bool saturated = (r_lo >= R) || (r_hi <= -R);
+        tmem_ld_x128_f2(tS, x2);
+        if (row == 0) TR(200 + 16 * t + 8 * g + 1);
+        tc_fence_before();
+        mbar_arrive(&s_consumed[g]);
+        // The key mask (additive, per key) joins the bias operand of the single FMA pass;
+        // tiles whose mask is all zero skip it.
+        const bool kadd = has_mask && !kzero[t % kStages];
+        const float2* kb2 = reinterpret_cast<const float2*>(kbias + (t % kStages) * kBN);
+        if (saturated) {
+          const float cb = rbias[(r_lo >= R ? 2 * R : 0) + kRPad];
+          const float2 cb2 = make_float2(cb, cb);
+          if (kadd) {
+#pragma unroll
+            for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(cb2, kb2[j]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, cb2);
+          }
+        } else {
+          const float* rb = rbias + (k0 - m + R + kRPad);   // rb[c] = bias of column c
+          if (kadd) {
+#pragma unroll
+            for (int j = 0; j < kBN / 2; ++j)
+              x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(make_float2(rb[2 * j], rb[2 * j + 1]), kb2[j]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, make_float2(rb[2 * j], rb[2 * j + 1]));
+          }
+        }
+        if (k0 + kBN > p.N || (p.causal && r_hi > 0)) {
+#pragma unroll
+          for (int j = 0; j < kBN / 2; ++j) {
+            const int n = k0 + 2 * j;
+            if (n >= p.N || (p.causal && n > m)) x2[j].x = -INFINITY;
+            if (n + 1 >= p.N || (p.causal && n + 1 > m)) x2[j].y = -INFINITY;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int ch = 0; ch < kBN / 32; ++ch) {
+          uint32_t sr[32];
+          tmem_ld_x32(tS + 32 * ch, sr);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int c = 32 * ch + i;
+            const int n = k0 + c;
+            float xv = -INFINITY;
+            if (n < klen) {
+              float acc = __uint_as_float(sr[i]);
+              const int r = min(max(m - n, -R), R);
+              const int idx = lut_s[r + R];
+              if (pk_row != nullptr) acc += to_f<T>(pk_row[idx * p.pk_sk]);
+              if (pq_base != nullptr) acc += to_f<T>(pq_base[(long long)n * p.pq_sn + idx * p.pq_sk]);
+              xv = acc * scale_log2;
+              if (p.causal && n > m + p.p_seq) xv = -INFINITY;
+            }
+            if (i & 1) x2[c >> 1].y = xv; else x2[c >> 1].x = xv;
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&s_consumed[g]);
+      }
+      if (row == 0) TR(200 + 16 * t + 8 * g + 2);
+      // Row max: four independent 3-input max chains.
+      float mx;
+      {
+        float a[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = fmaxf(x2[i].x, x2[i].y);
+#pragma unroll
+        for (int j = 4; j < kBN / 2; j += 4) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) a[i] = fmax3(a[i], x2[j + i].x, x2[j + i].y);
+        }
+        mx = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3]));
+      }
+
+      // Online softmax with lazy rescaling: the running max only moves (and O, l are
+      // rescaled) when a row's max grows by more than kRescaleThreshold.
+      const float m_new = fmaxf(m_run, mx);
+      const bool need = m_new > m_run + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, need)) {
+        const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
+        if (t > 0) {
+          // O holds PV(t-1) only once that MMA has completed.
+          const bool okp = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
+          if (!__all_sync(0xffffffffu, okp)) { aborted = true; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int ch = 0; ch < kHeadDim / 16; ++ch) {
+            uint32_t o[16];
+            tmem_ld_x16(tO + 16 * ch, o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_x16(tO + 16 * ch, o);
+          }
+        }
+        l_run *= alpha;
+        if (need) m_run = m_new;
+      }
+      if (row == 0) TR(200 + 16 * t + 8 * g + 3);
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      const float2 neg_m2 = make_float2(-m_use, -m_use);
+      uint32_t pk[kBN / 2];
+      float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < kBN / 2; ++j) {
+        const float2 y = __fadd2_rn(x2[j], neg_m2);
+        // One pair in kPolyEvery goes to the FMA pipe, the rest to the MUFU unit.
+        const float2 e = (j % kPolyEvery == kPolyEvery - 1) ? exp2_poly2(y)
+                                                            : make_float2(ex2_approx(y.x), ex2_approx(y.y));
+        if (j & 1) ls1 = __fadd2_rn(ls1, e); else ls0 = __fadd2_rn(ls0, e);
+        pk[j] = pack2<T>(e.x, e.y);
+      }
+      const float2 ls = __fadd2_rn(ls0, ls1);
+      l_run += ls.x + ls.y;
+      if (t > 0) {
+        // P(t-1) is read by PV(t-1): the P columns are free once it has completed.
+        const bool okp = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, okp)) { aborted = true; break; }
+        tc_fence_after();
+      }
+      if (row == 0) TR(200 + 16 * t + 8 * g + 4);
+      tmem_st_x64(tP, pk);
+      tc_fence_before();
+      mbar_arrive(&p_full[g]);
+      if (row == 0) TR(200 + 16 * t + 8 * g + 5);
+    }
+
+    // Epilogue: O / l, rows past the valid length written as zeros (DeBERTa).  The wait
+    // and the TMEM load are warp-collective and run on every lane (`aborted` and `nkv` are
+    // warp-uniform); only the global store depends on the lane's row.
+    uint32_t o[kHeadDim];
+    bool have = false;
+    if (nkv > 0 && !aborted) {
+      const bool ok = mbar_wait(&pv_done[g], (nkv - 1) & 1, abort_flag);
+      if (__all_sync(0xffffffffu, ok)) {
+        tc_fence_after();
+        tmem_ld_x64(tO, o);
+        have = true;
+      }
+    }
+    if (row == 0) TR(190 + g);
+    if (m < p.M) {
+      T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * p.o_sh + (long long)m * p.o_sm;
+      const bool row_valid = (kVariant != kDeberta) || (m < qlen);
+      const bool use = have && row_valid && l_run > 0.f;
+      const float inv_l = use ? 1.f / l_run : 0.f;
+#pragma unroll
+      for (int i = 0; i < kHeadDim / 8; ++i) {
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = use ? __uint_as_float(o[8 * i + j]) * inv_l : 0.f;
+        uint4 v;
+        v.x = pack2<T>(f[0], f[1]);
+        v.y = pack2<T>(f[2], f[3]);
+        v.z = pack2<T>(f[4], f[5]);
+        v.w = pack2<T>(f[6], f[7]);
+        *reinterpret_cast<uint4*>(orow + 8 * i) = v;
+      }
+    }
+  }
+
+  tc_fence_before();
+  named_bar_sync(1, 2 * 128 + 32);
+}
+
+}  // namespace vf
+
+// =====================================================================================
+// Host side: validation, bucket tables, tensor maps, launch, C ABI.
+// =====================================================================================
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int elem_size(vf_dtype_t d) { return d == VF_DTYPE_F32 ? 4 : 2; }
+
+// T5 relative bucket, float32 arithmetic in the reference's order of operations
+// (models/mt5/mt5_encoder.py:125-148).
+int t5_bucket_one(int rp, int num_buckets, int max_distance, bool bidirectional) {
+  int ret = 0;
+  int nb = num_buckets;
+  if (bidirectional) {
+    nb /= 2;
+    if (rp > 0) ret += nb;
+    rp = rp < 0 ? -rp : rp;
+  } else {
+    rp = rp < 0 ? -rp : 0;
+  }
+  const int max_exact = nb / 2;
+  if (rp < max_exact) return ret + rp;
+  const float num = logf(static_cast<float>(rp) / static_cast<float>(max_exact));
+  const float den = logf(static_cast<float>(static_cast<double>(max_distance) / static_cast<double>(max_exact)));
+  const float v = num / den * static_cast<float>(nb - max_exact);
+  long long large = max_exact + static_cast<long long>(v);   // .to(torch.long): truncation
+  if (large > nb - 1) large = nb - 1;
+  return ret + static_cast<int>(large);
+}
+
+// DeBERTa log bucket, float32 arithmetic in the reference's order of operations
+// (models/deberta_v2/deberta_v2_encoder.py:70-89).
+int deberta_bucket_one(int r, int bucket_size, int max_position) {
+  const int mid = bucket_size / 2;
+  const int sign = (r > 0) - (r < 0);
+  const int abs_pos = (r < mid && r > -mid) ? mid - 1 : (r < 0 ? -r : r);
+  if (abs_pos <= mid) return r;
+  const float num = logf(static_cast<float>(abs_pos) / static_cast<float>(mid));
+  const float den = logf(static_cast<float>(static_cast<double>(max_position - 1) / static_cast<double>(mid)));
+  const float lp = ceilf(num / den * static_cast<float>(mid - 1)) + static_cast<float>(mid);
+  return static_cast<int>(lp * static_cast<float>(sign));
+}
+
+// Cached relative-position tables.  `lut[i]` is the value for relative position i - R.
+struct RelTable {
+  int R = 0;
+  std::vector<short> lut;
+};
+std::mutex g_table_mu;
+std::map<std::tuple<int, int, int, int, int, int>, RelTable> g_tables;
+
+// Smallest radius R (<= rmax) such that f(r) == f(+-R) for every |r| in [R, rmax].
+template <class F>
+int saturation_radius(F f, int rmax) {
+  int R = rmax;
+  const int vpos = f(rmax), vneg = f(-rmax);
+  while (R > 0 && f(R - 1) == vpos && f(-(R - 1)) == vneg) --R;
+  return R;
+}
+
+const RelTable& t5_table(int nb, int maxd, bool bidir, int L) {
+  std::lock_guard<std::mutex> lk(g_table_mu);
+  auto key = std::make_tuple(0, nb, maxd, bidir ? 1 : 0, L, 0);
+  auto it = g_tables.find(key);
+  if (it != g_tables.end()) return it->second;
+  auto f = [&](int r) { return t5_bucket_one(r, nb, maxd, bidir); };
+  RelTable t;
+  t.R = saturation_radius(f, std::max(L - 1, 0));
+  t.lut.resize(2 * t.R + 1);
+  for (int i = 0; i <= 2 * t.R; ++i) t.lut[i] = static_cast<short>(f(i - t.R));
+  return g_tables.emplace(key, std::move(t)).first->second;
+}
+
+const RelTable& deberta_table(int span, int nbuckets, int maxd, bool log_bucket, int L) {
+  std::lock_guard<std::mutex> lk(g_table_mu);
+  auto key = std::make_tuple(1, span, nbuckets, maxd, log_bucket ? 1 : 0, L);
+  auto it = g_tables.find(key);
+  if (it != g_tables.end()) return it->second;
+  auto f = [&](int r) {
+    const int bucket = log_bucket ? deberta_bucket_one(r, nbuckets, maxd) : r;
+    long long idx = static_cast<long long>(bucket) + span;
+    if (idx < 0) idx = 0;
+    if (idx > 2LL * span - 1) idx = 2LL * span - 1;
+    return static_cast<int>(idx);
+  };
+  RelTable t;
+  t.R = saturation_radius(f, std::max(L - 1, 0));
+  t.lut.resize(2 * t.R + 1);
+  for (int i = 0; i <= 2 * t.R; ++i) t.lut[i] = static_cast<short>(f(i - t.R));
+  return g_tables.emplace(key, std::move(t)).first->second;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// (B, H, L, 64) strided view -> 4-D tensor map with a 64 x 128 box, 128-byte swizzle.
+int make_tile_map(CUtensorMap* map, const vf_tensor4d_t& t, vf_dtype_t dt, const char* name) {
+  auto enc = get_encode_fn();
+  if (enc == nullptr) return fail(VF_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const int es = elem_size(dt);
+  if (t.stride[3] != 1) return fail(VF_EINVAL, std::string(name) + ": innermost (head_dim) stride must be 1");
+  if ((reinterpret_cast<uintptr_t>(t.data) & 15) != 0) return fail(VF_EINVAL, std::string(name) + ": base pointer must be 16-byte aligned");
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(t.size[3]), static_cast<cuuint64_t>(t.size[2]),
+                        static_cast<cuuint64_t>(t.size[1]), static_cast<cuuint64_t>(t.size[0])};
+  cuuint64_t strides[3];
+  for (int i = 0; i < 3; ++i) {
+    const long long s = t.stride[2 - i] * es;
+    if (s <= 0 || (s % 16) != 0) return fail(VF_EINVAL, std::string(name) + ": strides must be positive multiples of 16 bytes");
+    strides[i] = static_cast<cuuint64_t>(s);
+  }
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType ty = dt == VF_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, ty, 4, const_cast<void*>(t.data), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(VF_ECUDA, std::string(name) + ": cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return VF_OK;
+}
+
+int check_qkv(const vf_tensor4d_t& q, const vf_tensor4d_t& k, const vf_tensor4d_t& v, const vf_tensor4d_t& o) {
+  if (!q.data || !k.data || !v.data || !o.data) return fail(VF_EINVAL, "q, k, v and out must be non-null");
+  for (int i = 0; i < 4; ++i)
+    if (q.size[i] <= 0 || k.size[i] <= 0 || v.size[i] <= 0) return fail(VF_EINVAL, "q, k, v must have positive sizes");
+  if (q.size[3] != vf::kHeadDim || k.size[3] != vf::kHeadDim || v.size[3] != vf::kHeadDim)
+    return fail(VF_EUNSUPPORTED, "head_dim must be 64");
+  if (k.size[0] != q.size[0] || v.size[0] != q.size[0] || k.size[1] != q.size[1] || v.size[1] != q.size[1])
+    return fail(VF_EINVAL, "q, k, v must agree on batch and heads");
+  if (v.size[2] != k.size[2]) return fail(VF_EINVAL, "k and v must have the same length");
+  for (int i = 0; i < 4; ++i)
+    if (o.size[i] != q.size[i]) return fail(VF_EINVAL, "out must have the shape of q");
+  if (o.stride[3] != 1 || (o.stride[2] % 8) != 0 || (reinterpret_cast<uintptr_t>(o.data) & 15) != 0)
+    return fail(VF_EINVAL, "out rows must be contiguous and 16-byte aligned");
+  if (q.size[0] > 65535 || q.size[1] > 65535) return fail(VF_EUNSUPPORTED, "batch and heads must be < 65536");
+  if (q.size[2] > (1 << 30) || k.size[2] > (1 << 30)) return fail(VF_EUNSUPPORTED, "sequence too long");
+  return VF_OK;
+}
+
+template <int kVariant, typename T>
+int launch(vf::KParams* kp, cudaStream_t stream) {
+  auto kern = vf::attn_fwd_kernel<kVariant, T>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::once_flag flags[64];
+  static cudaError_t attr_err[64];
+  if (dev < 0 || dev >= 64) return fail(VF_ECUDA, "device ordinal out of range");
+  std::call_once(flags[dev], [&] {
+    attr_err[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, vf::kSmemAlloc);
+  });
+  if (attr_err[dev] != cudaSuccess) return fail(VF_ECUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err[dev]));
+  dim3 grid((kp->M + vf::kNQ * vf::kBM - 1) / (vf::kNQ * vf::kBM), kp->H, kp->B);
+  kern<<<grid, vf::kThreads, vf::kSmemAlloc, stream>>>(*kp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(VF_ECUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  return VF_OK;
+}
+
+void fill_common(vf::KParams* kp, const vf_tensor4d_t& q, const vf_tensor4d_t& k, const vf_tensor4d_t& o) {
+  kp->out = const_cast<void*>(o.data);
+  kp->o_sb = o.stride[0];
+  kp->o_sh = o.stride[1];
+  kp->o_sm = o.stride[2];
+  kp->B = static_cast<int>(q.size[0]);
+  kp->H = static_cast<int>(q.size[1]);
+  kp->M = static_cast<int>(q.size[2]);
+  kp->N = static_cast<int>(k.size[2]);
+}
+
+}  // namespace
+
+extern "C" {
+int vf_trace_read(long long* out, int n) { return (int)cudaMemcpyFromSymbol(out, vf::g_trace, n * sizeof(long long)); }
+
+const char* vf_last_error(void) { return g_last_error.c_str(); }
+
+int vf_abi_version(void) { return VF_ABI_VERSION; }
+
+int vf_device_error(int32_t clear) {
+  unsigned int word = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(VF_ECUDA, std::string("cudaDeviceSynchronize: ") + cudaGetErrorString(e));
+  e = cudaMemcpyFromSymbol(&word, vf::g_vf_error, sizeof(word));
+  if (e != cudaSuccess) return fail(VF_ECUDA, std::string("cudaMemcpyFromSymbol: ") + cudaGetErrorString(e));
+  if (clear) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(vf::g_vf_error, &zero, sizeof(zero));
+    if (e != cudaSuccess) return fail(VF_ECUDA, std::string("cudaMemcpyToSymbol: ") + cudaGetErrorString(e));
+  }
+  return static_cast<int>(word & 0x7fffffff);
+}
+
+int vf_t5_relative_bucket(int32_t num_buckets, int32_t max_distance, int32_t bidirectional, int32_t rmin,
+                          int32_t rmax, int32_t* out) {
+  if (out == nullptr || rmax < rmin) return fail(VF_EINVAL, "bad output range");
+  const int half = bidirectional ? num_buckets / 2 : num_buckets;
+  if (half / 2 < 1) return fail(VF_EUNSUPPORTED, "num_buckets too small for the T5 bucket formula");
+  if (max_distance <= half / 2) return fail(VF_EUNSUPPORTED, "max_distance must exceed num_buckets/4 (bidirectional) or num_buckets/2");
+  for (int r = rmin; r <= rmax; ++r) out[r - rmin] = t5_bucket_one(r, num_buckets, max_distance, bidirectional != 0);
+  return VF_OK;
+}
+
+int vf_deberta_log_bucket(int32_t bucket_size, int32_t max_position, int32_t rmin, int32_t rmax, int32_t* out) {
+  if (out == nullptr || rmax < rmin) return fail(VF_EINVAL, "bad output range");
+  if (bucket_size < 4 || max_position - 1 <= bucket_size / 2)
+    return fail(VF_EUNSUPPORTED, "log buckets need bucket_size >= 4 and max_position - 1 > bucket_size / 2");
+  for (int r = rmin; r <= rmax; ++r) out[r - rmin] = deberta_bucket_one(r, bucket_size, max_position);
+  return VF_OK;
+}
+
+int vf_rpb_attention_fwd(const vf_rpb_attention_args_t* a, void* stream) {
+  if (a == nullptr) return fail(VF_EINVAL, "null args");
+  if (a->dtype != VF_DTYPE_BF16 && a->dtype != VF_DTYPE_F16)
+    return fail(VF_EUNSUPPORTED, "rpb attention: q/k/v dtype must be float16 or bfloat16");
+  int rc = check_qkv(a->q, a->k, a->v, a->out);
+  if (rc) return rc;
+  if (a->dropout_p != 0.0f) return fail(VF_EUNSUPPORTED, "rpb attention: dropout_p must be 0 (inference path)");
+  const int H = static_cast<int>(a->q.size[1]);
+  const int M = static_cast<int>(a->q.size[2]), N = static_cast<int>(a->k.size[2]);
+  static thread_local vf::KParams kp;
+  std::memset(&kp, 0, offsetof(vf::KParams, lut));
+  if ((rc = make_tile_map(&kp.tm_q, a->q, a->dtype, "q"))) return rc;
+  if ((rc = make_tile_map(&kp.tm_k, a->k, a->dtype, "k"))) return rc;
+  if ((rc = make_tile_map(&kp.tm_v, a->v, a->dtype, "v"))) return rc;
+  fill_common(&kp, a->q, a->k, a->out);
+  kp.scale_log2 = a->softmax_scale * vf::kLog2e;
+  kp.causal = a->is_decoder ? 1 : 0;
+  kp.p_seq = 0;
+  if (a->rpb_table != nullptr) {
+    if (a->table_cols != H) return fail(VF_EINVAL, "rpb_table must be [num_buckets, heads]");
+    if (a->table_rows <= 0) return fail(VF_EINVAL, "rpb_table has no rows");
+    kp.table = a->rpb_table;
+    kp.tb_srow = a->table_stride_row;
+    kp.tb_scol = a->table_stride_col;
+    kp.table_dtype = a->table_dtype;
+  }
+  const int nb = static_cast<int>(a->rpb_table ? a->table_rows : a->num_buckets);
+  {
+    const int half = a->is_decoder ? a->num_buckets : a->num_buckets / 2;
+    if (half / 2 < 1 || a->max_distance <= half / 2)
+      return fail(VF_EUNSUPPORTED, "rpb attention: bucket configuration outside the T5 formula's domain");
+  }
+  const RelTable& tab = t5_table(a->num_buckets, a->max_distance, !a->is_decoder, std::max(M, N));
+  if (tab.R > vf::kMaxRel) return fail(VF_EUNSUPPORTED, "rpb attention: relative-position table too large");
+  kp.rel_R = tab.R;
+  for (int i = 0; i <= 2 * tab.R; ++i) {
+    int v = tab.lut[i];
+    v = std::min(std::max(v, 0), nb - 1);   // kernels/flash_attention_rpb.py:162 clamp to the table
+    kp.lut[i] = static_cast<short>(v);
+  }
+  if (a->padding_mask.data != nullptr) {
+    const vf_tensor4d_t& mk = a->padding_mask;
+    if (mk.size[2] != 1 && mk.stride[2] != 0)
+      return fail(VF_EUNSUPPORTED, "rpb attention: padding_mask must broadcast over query rows ([B|1, H|1, 1, N])");
+    if (mk.size[3] != N) return fail(VF_EINVAL, "rpb attention: padding_mask last dim must equal key length");
+    if (mk.size[0] != 1 && mk.size[0] != a->q.size[0]) return fail(VF_EINVAL, "rpb attention: padding_mask batch dim");
+    if (mk.size[1] != 1 && mk.size[1] != H) return fail(VF_EINVAL, "rpb attention: padding_mask head dim");
+    kp.mask = mk.data;
+    kp.mk_sb = mk.size[0] > 1 ? mk.stride[0] : 0;
+    kp.mk_sh = mk.size[1] > 1 ? mk.stride[1] : 0;
+    kp.mk_sn = mk.size[3] > 1 ? mk.stride[3] : 0;
+    kp.mask_dtype = a->mask_dtype;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return a->dtype == VF_DTYPE_BF16 ? launch<vf::kT5, __nv_bfloat16>(&kp, s) : launch<vf::kT5, __half>(&kp, s);
+}
+
+int vf_deberta_attention_fwd(const vf_deberta_attention_args_t* a, void* stream) {
+  if (a == nullptr) return fail(VF_EINVAL, "null args");
+  if (a->dtype != VF_DTYPE_BF16 && a->dtype != VF_DTYPE_F16)
+    return fail(VF_EUNSUPPORTED, "deberta attention: q/k/v dtype must be float16 or bfloat16");
+  int rc = check_qkv(a->q, a->k, a->v, a->out);
+  if (rc) return rc;
+  const int B = static_cast<int>(a->q.size[0]), H = static_cast<int>(a->q.size[1]);
+  const int M = static_cast<int>(a->q.size[2]), N = static_cast<int>(a->k.size[2]);
+  const int span = a->position_buckets > 0 ? a->position_buckets : a->max_relative_distance;
+  const bool has_pos = a->pos_key.data != nullptr || a->pos_query.data != nullptr;
+  if (has_pos && span <= 0) return fail(VF_EINVAL, "deberta attention: position terms need position_buckets or max_relative_distance > 0");
+  static thread_local vf::KParams kp;
+  std::memset(&kp, 0, offsetof(vf::KParams, lut));
+  if ((rc = make_tile_map(&kp.tm_q, a->q, a->dtype, "q"))) return rc;
+  if ((rc = make_tile_map(&kp.tm_k, a->k, a->dtype, "k"))) return rc;
+  if ((rc = make_tile_map(&kp.tm_v, a->v, a->dtype, "v"))) return rc;
+  fill_common(&kp, a->q, a->k, a->out);
+  const float sm_scale = a->has_sm_scale ? a->sm_scale : 1.0f / std::sqrt(static_cast<float>(vf::kHeadDim));
+  kp.scale_log2 = sm_scale * vf::kLog2e;
+  kp.causal = a->causal ? 1 : 0;
+  kp.p_seq = N - M;
+  kp.seq_lengths = a->seq_lengths;
+  kp.span2 = 2 * span;
+  if (a->pos_key.data != nullptr) {
+    const vf_tensor4d_t& t = a->pos_key;
+    if (t.size[0] != B || t.size[1] != H || t.size[2] != M || t.size[3] < 2 * span)
+      return fail(VF_EINVAL, "deberta attention: pos_key must be (B, H, M, 2*ATT_SPAN)");
+    kp.pos_key = t.data;
+    kp.pk_sb = t.stride[0]; kp.pk_sh = t.stride[1]; kp.pk_sm = t.stride[2]; kp.pk_sk = t.stride[3];
+  }
+  if (a->pos_query.data != nullptr) {
+    const vf_tensor4d_t& t = a->pos_query;
+    if (t.size[0] != B || t.size[1] != H || t.size[2] != N || t.size[3] < 2 * span)
+      return fail(VF_EINVAL, "deberta attention: pos_query must be (B, H, N, 2*ATT_SPAN)");
+    kp.pos_query = t.data;
+    kp.pq_sb = t.stride[0]; kp.pq_sh = t.stride[1]; kp.pq_sn = t.stride[2]; kp.pq_sk = t.stride[3];
+  }
+  // Log buckets exactly when the reference's torch path uses them
+  // (kernels/flash_deberta_attention.py:400).
+  const bool log_bucket = a->use_log_bucket && a->position_buckets > 0 && a->max_relative_distance > 0;
+  if (log_bucket && (a->position_buckets < 4 || a->max_relative_distance - 1 <= a->position_buckets / 2))
+    return fail(VF_EUNSUPPORTED, "deberta attention: log-bucket configuration outside the formula's domain");
+  if (has_pos) {
+    const RelTable& tab = deberta_table(span, a->position_buckets, a->max_relative_distance, log_bucket, std::max(M, N));
+    if (tab.R > vf::kMaxRel) return fail(VF_EUNSUPPORTED, "deberta attention: relative-position table too large");
+    kp.rel_R = tab.R;
+    std::memcpy(kp.lut, tab.lut.data(), tab.lut.size() * sizeof(short));
+  } else {
+    kp.rel_R = 0;
+    kp.lut[0] = 0;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return a->dtype == VF_DTYPE_BF16 ? launch<vf::kDeberta, __nv_bfloat16>(&kp, s) : launch<vf::kDeberta, __half>(&kp, s);
+}
+
+}  // extern "C"

@@ -57,6 +57,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kDeadMask = -1.0e4f;        // additive mask at/below this kills a key
 constexpr float kMaskFloor = -1.0e30f;      // masks are clamped here before scaling
 constexpr float kRescaleThreshold = 8.0f;   // lazy O rescale (log2 units)
+constexpr int kPolyEvery = 3;               // every 3rd exponential pair on the FMA pipe
 
 enum Variant : int { kT5 = 0, kDeberta = 1 };
 
@@ -96,8 +97,9 @@ constexpr int kOffKZero = kOffKBias + kStages * kBN * 4;         // per stage: k
 constexpr int kOffRBias = kOffKZero + 16;
 constexpr int kOffLut = kOffRBias + (kMaxLut + 2 * kRPad) * 4 + 12;   // keep 16-byte alignment
 constexpr int kOffBar = (kOffLut + kMaxLut * 2 + 15 + 64) & ~15;
-// barriers: q_full, s_full[2], p_full[2], o_full, k_full[3], v_full[3], kv_empty[3], drain
-constexpr int kNumBars = 1 + 2 + 2 + 1 + 3 * kStages + 1;
+// barriers: q_full, s_full[2], p_full[2], s_consumed[2], pv_done[2], k_full[3], v_full[3],
+// kv_empty[3], drain
+constexpr int kNumBars = 1 + 2 + 2 + 2 + 2 + 3 * kStages + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 64;
 constexpr int kSmemAlloc = kSmemBytes + 1024;
@@ -149,10 +151,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   short* lut_s = reinterpret_cast<short*>(smem + kOffLut);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* s_full = bars + 1;        // [2]
-  uint64_t* p_full = bars + 3;        // [2]
-  uint64_t* o_full = bars + 5;
-  uint64_t* k_full = bars + 6;        // [kStages]
+  uint64_t* s_full = bars + 1;        // [2] S = Q K^T of the tile is in TMEM
+  uint64_t* p_full = bars + 3;        // [2] P of the tile is in TMEM
+  uint64_t* s_consumed = bars + 5;    // [2] softmax has read S into registers
+  uint64_t* pv_done = bars + 7;       // [2] O += P V of the tile has completed
+  uint64_t* k_full = bars + 9;        // [kStages]
   uint64_t* v_full = k_full + kStages;
   uint64_t* kv_empty = v_full + kStages;
   uint64_t* drain = kv_empty + kStages;
@@ -182,8 +185,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   const bool has_mask = (kVariant == kT5) && (p.mask != nullptr);
   if (tid == 0) {
     mbar_init(q_full, 1);
-    for (int g = 0; g < kNQ; ++g) { mbar_init(&s_full[g], 1); mbar_init(&p_full[g], kBM); }
-    mbar_init(o_full, 1);
+    for (int g = 0; g < kNQ; ++g) {
+      mbar_init(&s_full[g], 1);
+      mbar_init(&p_full[g], kBM);
+      mbar_init(&s_consumed[g], kBM);
+      mbar_init(&pv_done[g], 1);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&k_full[s], has_mask ? 2 : 1);
       mbar_init(&v_full[s], 1);
@@ -194,6 +201,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     misc->live_lo = 0x7fffffff;
     misc->live_hi = -1;
     fence_mbar_init();
+    // Q does not depend on the key range: start its copy before the prologue work.
+    mbar_arrive_expect_tx(q_full, kNQ * kTileBytes);
+    for (int g = 0; g < kNQ; ++g)
+      tma_load_4d(smem + kOffQ + g * kTileBytes, &p.tm_q, q_full, 0, q0 + g * kBM, h, b);
   }
   if (warp == kMmaWarp) {
     tmem_alloc(&misc->tmem_base, kTmemCols);
@@ -248,11 +259,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   reg_dealloc<kRegsProducer>();
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && nkv > 0) {
-      mbar_arrive_expect_tx(q_full, kNQ * kTileBytes);
-      for (int g = 0; g < kNQ; ++g)
-        tma_load_4d(smem + kOffQ + g * kTileBytes, &p.tm_q, q_full, 0, q0 + g * kBM, h, b);
-    }
     int issued = 0;
     for (int t = 0; t < nkv; ++t) {
       const int s = t % kStages;
@@ -288,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     }
     // No TMA write may land after this CTA exits: wait for the last fills (already
     // complete on the normal path), ignoring the abort flag but still time-bounded.
-    if (lane == 0 && nkv > 0) {
+    if (lane == 0) {
       mbar_wait_bounded(q_full, 0);
       for (int t = max(issued - kStages, 0); t < issued; ++t) {
         mbar_wait_bounded(&k_full[t % kStages], (t / kStages) & 1);
@@ -320,6 +326,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
                   (acc || kk > 0) ? 1u : 0u);
         }
       };
+      // Order per key tile t: as soon as a group has read S(t) into registers, its
+      // S(t+1) = Q K(t+1)^T is issued (it overlaps that group's exponentials); PV(t) is
+      // issued when the group's P(t) is in TMEM.
       bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
       if (ok) {
         tc_fence_after();
@@ -329,28 +338,32 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         umma_commit(&s_full[1]);
         for (int t = 0; t < nkv; ++t) {
           const int s = t % kStages;
-          if (!mbar_wait(&v_full[s], (t / kStages) & 1, abort_flag)) break;
-          if (!mbar_wait(&p_full[0], t & 1, abort_flag)) break;
-          tc_fence_after();
-          issue_pv(0, s, t > 0);
           const bool has_next = t + 1 < nkv;
           const int s2 = (t + 1) % kStages;
+          if (has_next && !mbar_wait(&k_full[s2], ((t + 1) / kStages) & 1, abort_flag)) break;
+          if (!mbar_wait(&s_consumed[0], t & 1, abort_flag)) break;
           if (has_next) {
-            if (!mbar_wait(&k_full[s2], ((t + 1) / kStages) & 1, abort_flag)) break;
             tc_fence_after();
             issue_qk(0, s2);
             umma_commit(&s_full[0]);
           }
-          if (!mbar_wait(&p_full[1], t & 1, abort_flag)) break;
-          tc_fence_after();
-          issue_pv(1, s, t > 0);
-          umma_commit(&kv_empty[s]);
+          if (!mbar_wait(&s_consumed[1], t & 1, abort_flag)) break;
           if (has_next) {
+            tc_fence_after();
             issue_qk(1, s2);
             umma_commit(&s_full[1]);
           }
+          if (!mbar_wait(&v_full[s], (t / kStages) & 1, abort_flag)) break;
+          if (!mbar_wait(&p_full[0], t & 1, abort_flag)) break;
+          tc_fence_after();
+          issue_pv(0, s, t > 0);
+          umma_commit(&pv_done[0]);
+          if (!mbar_wait(&p_full[1], t & 1, abort_flag)) break;
+          tc_fence_after();
+          issue_pv(1, s, t > 0);
+          umma_commit(&pv_done[1]);
+          umma_commit(&kv_empty[s]);
         }
-        umma_commit(o_full);
       }
       // Drain: every MMA issued above has completed before TMEM is released.
       umma_commit(drain);
@@ -405,6 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       // pressure; the asm's memory clobber also keeps each chunk's loads behind its TMEM
       // load).  x2[j] holds columns 2j, 2j+1.
       float2 x2[kBN / 2];
+      bool const_bias = false;   // x2 holds raw S; bias `cbias` and scale still to apply
+      float cbias = 0.f;
       if constexpr (kVariant == kT5) {
         // Warp-uniform tile class over the warp's 32 rows: r = n - m in [r_lo, r_hi].
         const int m0 = m - lane;
@@ -413,11 +428,19 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         const float2 sc2 = make_float2(scale_log2, scale_log2);
         const bool saturated = (r_lo >= R) || (r_hi <= -R);
         tmem_ld_x128_f2(tS, x2);
+        tc_fence_before();
+        mbar_arrive(&s_consumed[g]);
         // The key mask (additive, per key) joins the bias operand of the single FMA pass;
         // tiles whose mask is all zero skip it.
         const bool kadd = has_mask && !kzero[t % kStages];
         const float2* kb2 = reinterpret_cast<const float2*>(kbias + (t % kStages) * kBN);
-        if (saturated) {
+        const bool edge = (k0 + kBN > p.N) || (p.causal && r_hi > 0);
+        if (saturated && !kadd && !edge && scale_log2 > 0.f) {
+          // Constant bias: keep raw S; max(s * sc + cb) = max(s) * sc + cb, and the
+          // exponent pass computes s * sc + (cb - m) in one FMA.
+          const_bias = true;
+          cbias = rbias[(r_lo >= R ? 2 * R : 0) + kRPad];
+        } else if (saturated) {
           const float cb = rbias[(r_lo >= R ? 2 * R : 0) + kRPad];
           const float2 cb2 = make_float2(cb, cb);
           if (kadd) {
@@ -438,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, make_float2(rb[2 * j], rb[2 * j + 1]));
           }
         }
-        if (k0 + kBN > p.N || (p.causal && r_hi > 0)) {
+        if (edge) {
 #pragma unroll
           for (int j = 0; j < kBN / 2; ++j) {
             const int n = k0 + 2 * j;
@@ -468,19 +491,22 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             if (i & 1) x2[c >> 1].y = xv; else x2[c >> 1].x = xv;
           }
         }
+        tc_fence_before();
+        mbar_arrive(&s_consumed[g]);
       }
-      // Row max: four independent 3-input max chains.
+      // Row max: eight independent 3-input max chains.
       float mx;
       {
-        float a[4];
+        float a[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) a[i] = fmaxf(x2[i].x, x2[i].y);
+        for (int i = 0; i < 8; ++i) a[i] = fmaxf(x2[i].x, x2[i].y);
 #pragma unroll
-        for (int j = 4; j < kBN / 2; j += 4) {
+        for (int j = 8; j < kBN / 2; j += 8) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) a[i] = fmax3(a[i], x2[j + i].x, x2[j + i].y);
+          for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], x2[j + i].x, x2[j + i].y);
         }
-        mx = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3]));
+        mx = fmaxf(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], fmax3(a[5], a[6], a[7])));
+        if (const_bias) mx = fmaf(mx, scale_log2, cbias);
       }
 
       // Online softmax with lazy rescaling: the running max only moves (and O, l are
@@ -490,6 +516,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       if (__any_sync(0xffffffffu, need)) {
         const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
         if (t > 0) {
+          // O holds PV(t-1) only once that MMA has completed.
+          const bool okp = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
+          if (!__all_sync(0xffffffffu, okp)) { aborted = true; break; }
+          tc_fence_after();
 #pragma unroll
           for (int ch = 0; ch < kHeadDim / 16; ++ch) {
             uint32_t o[16];
@@ -503,19 +533,34 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         if (need) m_run = m_new;
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      const float2 neg_m2 = make_float2(-m_use, -m_use);
-      uint32_t pk[kBN / 2];
+      // y = x * mul + add: (1, -m) for finished scores, (scale, cbias - m) for raw S.
+      const float2 mul2 = const_bias ? make_float2(scale_log2, scale_log2) : make_float2(1.f, 1.f);
+      const float2 add2 = const_bias ? make_float2(cbias - m_use, cbias - m_use) : make_float2(-m_use, -m_use);
+      if (t > 0) {
+        // P(t-1) is read by PV(t-1): the P columns are free once it has completed.
+        const bool okp = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, okp)) { aborted = true; break; }
+        tc_fence_after();
+      }
       float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int j = 0; j < kBN / 2; ++j) {
-        const float2 y = __fadd2_rn(x2[j], neg_m2);
-        const float2 e = make_float2(ex2_approx(y.x), ex2_approx(y.y));
-        if (j & 1) ls1 = __fadd2_rn(ls1, e); else ls0 = __fadd2_rn(ls0, e);
-        pk[j] = pack2<T>(e.x, e.y);
+      for (int ch = 0; ch < kBN / 32; ++ch) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int j = 16 * ch + jj;
+          const float2 y = __ffma2_rn(x2[j], mul2, add2);
+          // One pair in kPolyEvery goes to the FMA pipe, the rest to the MUFU unit.
+          const float2 e = (j % kPolyEvery == kPolyEvery - 1) ? exp2_poly2(y)
+                                                              : make_float2(ex2_approx(y.x), ex2_approx(y.y));
+          if (j & 1) ls1 = __fadd2_rn(ls1, e); else ls0 = __fadd2_rn(ls0, e);
+          pk[jj] = pack2<T>(e.x, e.y);
+        }
+        tmem_st_x16_nowait(tP + 16 * ch, pk);
       }
       const float2 ls = __fadd2_rn(ls0, ls1);
       l_run += ls.x + ls.y;
-      tmem_st_x64(tP, pk);
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[g]);
     }
@@ -526,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     uint32_t o[kHeadDim];
     bool have = false;
     if (nkv > 0 && !aborted) {
-      const bool ok = mbar_wait(o_full, 0, abort_flag);
+      const bool ok = mbar_wait(&pv_done[g], (nkv - 1) & 1, abort_flag);
       if (__all_sync(0xffffffffu, ok)) {
         tc_fence_after();
         tmem_ld_x64(tO, o);

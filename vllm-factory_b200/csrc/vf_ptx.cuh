@@ -48,6 +48,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
   return ok != 0;
 }
+// As above, but the thread may sleep up to `suspend_ns` (it wakes when the phase
+// completes), so waiting warps do not take issue slots from working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok) : "r"(bar), "r"(parity), "r"(suspend_ns) : "memory");
+  return ok != 0;
+}
+constexpr uint32_t kSuspendNs = 20000;   // 20 us per sleep; the cycle bound still applies
 
 // Waits for the phase with the given parity to complete.  Every wait is bounded: after
 // kWaitCycles it sets the CTA abort flag and the global error word and returns false.  A
@@ -58,9 +70,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(a, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(a, parity)) return true;
+    if (mbar_try_wait_sleep(a, parity, kSuspendNs)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > kWaitCycles) {
       *abort_flag = 1;
@@ -224,6 +234,18 @@ __device__ __forceinline__ void tmem_ld_x128_f2(uint32_t taddr, float2 (&x)[64])
                : "r"(taddr) : "memory");
 }
 
+// tcgen05.st of 16 columns without waiting; the caller issues tmem_wait_st() before the
+// data is consumed.  The source registers are read when the instruction issues.
+__device__ __forceinline__ void tmem_st_x16_nowait(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n"
+               :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+                  "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- math helpers
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -253,6 +275,28 @@ template <uint32_t N> __device__ __forceinline__ void reg_alloc() {
 }
 template <uint32_t N> __device__ __forceinline__ void reg_dealloc() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" :: "n"(N));
+}
+
+// 2^y for a pair on the FMA pipe (offloads the MUFU unit, whose ex2 throughput caps
+// attention with 64-wide heads).  Method: y clamped to >= -125; y = j + f with
+// j = round(y) obtained from y + 1.5*2^23 (round-to-nearest in the float adder) and
+// f in [-0.5, 0.5]; 2^f by a degree-3 polynomial whose coefficients are a minimax fit of
+// the relative error over [-0.5, 0.5] (max relative error 7.5e-5, far below bf16/fp16
+// resolution); 2^j applied by adding j to the exponent field: the low mantissa bits of
+// y + 1.5*2^23 hold j, so (bits << 23) is j * 2^23 modulo 2^32.
+__device__ __forceinline__ float2 exp2_poly2(float2 y) {
+  constexpr float kRound = 12582912.0f;   // 1.5 * 2^23
+  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.05517167f;
+  y.x = fmaxf(y.x, -125.0f);
+  y.y = fmaxf(y.y, -125.0f);
+  const float2 t = __fadd2_rn(y, make_float2(kRound, kRound));
+  const float2 j = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), y);
+  float2 q = __ffma2_rn(make_float2(c3, c3), f, make_float2(c2, c2));
+  q = __ffma2_rn(q, f, make_float2(c1, c1));
+  q = __ffma2_rn(q, f, make_float2(c0, c0));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
 }
 
 // Named barrier over `nthreads` threads (a multiple of 32).
