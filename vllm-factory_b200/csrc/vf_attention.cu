@@ -536,31 +536,27 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       // y = x * mul + add: (1, -m) for finished scores, (scale, cbias - m) for raw S.
       const float2 mul2 = const_bias ? make_float2(scale_log2, scale_log2) : make_float2(1.f, 1.f);
       const float2 add2 = const_bias ? make_float2(cbias - m_use, cbias - m_use) : make_float2(-m_use, -m_use);
+      float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
+      uint32_t pk[kBN / 2];
+#pragma unroll
+      for (int j = 0; j < kBN / 2; ++j) {
+        const float2 y = __ffma2_rn(x2[j], mul2, add2);
+        // One pair in kPolyEvery goes to the FMA pipe, the rest to the MUFU unit.
+        const float2 e = (j % kPolyEvery == kPolyEvery - 1) ? exp2_poly2(y)
+                                                            : make_float2(ex2_approx(y.x), ex2_approx(y.y));
+        if (j & 1) ls1 = __fadd2_rn(ls1, e); else ls0 = __fadd2_rn(ls0, e);
+        pk[j] = pack2<T>(e.x, e.y);
+      }
+      const float2 ls = __fadd2_rn(ls0, ls1);
+      l_run += ls.x + ls.y;
       if (t > 0) {
-        // P(t-1) is read by PV(t-1): the P columns are free once it has completed.
+        // P(t-1) is read by PV(t-1): the P columns are free once it has completed.  The
+        // wait sits after the exponentials, so the PV round trip overlaps them.
         const bool okp = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, okp)) { aborted = true; break; }
         tc_fence_after();
       }
-      float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int ch = 0; ch < kBN / 32; ++ch) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int j = 16 * ch + jj;
-          const float2 y = __ffma2_rn(x2[j], mul2, add2);
-          // One pair in kPolyEvery goes to the FMA pipe, the rest to the MUFU unit.
-          const float2 e = (j % kPolyEvery == kPolyEvery - 1) ? exp2_poly2(y)
-                                                              : make_float2(ex2_approx(y.x), ex2_approx(y.y));
-          if (j & 1) ls1 = __fadd2_rn(ls1, e); else ls0 = __fadd2_rn(ls0, e);
-          pk[jj] = pack2<T>(e.x, e.y);
-        }
-        tmem_st_x16_nowait(tP + 16 * ch, pk);
-      }
-      const float2 ls = __fadd2_rn(ls0, ls1);
-      l_run += ls.x + ls.y;
-      tmem_wait_st();
+      tmem_st_x64(tP, pk);
       tc_fence_before();
       mbar_arrive(&p_full[g]);
     }
