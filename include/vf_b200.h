@@ -130,6 +130,13 @@ const char* vf_last_error(void);
  * Synchronises the device.  Returns the word (>= 0) or VF_ECUDA. */
 int vf_device_error(int32_t clear);
 
+/* Failure-detection self-test (no counterpart in the reference): launches one CTA whose
+ * bounded wait is on an mbarrier that nothing arrives at.  After `limit_cycles` SM cycles
+ * the wait gives up and sets bit 0 of the device error word (read it with
+ * vf_device_error); the kernel returns and the context stays usable.  Synchronises
+ * `stream`.  Returns 0 or a negative VF_E* code. */
+int vf_selftest_wait_timeout(int64_t limit_cycles, void* stream);
+
 /* VF_ABI_VERSION of the loaded library. */
 int vf_abi_version(void);
 

@@ -598,6 +598,22 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   named_bar_sync(1, 2 * 128 + 32);
 }
 
+// Failure-detection self-test: one CTA waits on an mbarrier that nothing ever arrives
+// at.  The bounded wait must give up after `limit_cycles`, set the abort flag and the
+// device error word, and return; the kernel then exits normally.
+__global__ void selftest_wait_timeout_kernel(long long limit_cycles, int* result) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(&bar, 0, &abort_flag, limit_cycles);
+  if (threadIdx.x == 0 && result != nullptr) *result = ok ? 1 : 0;
+}
+
 }  // namespace vf
 
 // =====================================================================================
@@ -803,6 +819,17 @@ int vf_device_error(int32_t clear) {
     if (e != cudaSuccess) return fail(VF_ECUDA, std::string("cudaMemcpyToSymbol: ") + cudaGetErrorString(e));
   }
   return static_cast<int>(word & 0x7fffffff);
+}
+
+int vf_selftest_wait_timeout(int64_t limit_cycles, void* stream) {
+  if (limit_cycles <= 0) return fail(VF_EINVAL, "limit_cycles must be positive");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  vf::selftest_wait_timeout_kernel<<<1, 32, 0, s>>>(static_cast<long long>(limit_cycles), nullptr);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(VF_ECUDA, std::string("selftest launch: ") + cudaGetErrorString(e));
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail(VF_ECUDA, std::string("selftest: ") + cudaGetErrorString(e));
+  return VF_OK;
 }
 
 int vf_t5_relative_bucket(int32_t num_buckets, int32_t max_distance, int32_t bidirectional, int32_t rmin,

@@ -65,14 +65,15 @@ constexpr uint32_t kSuspendNs = 20000;   // 20 us per sleep; the cycle bound sti
 // kWaitCycles it sets the CTA abort flag and the global error word and returns false.  A
 // wait also returns false as soon as another thread of the CTA has set the abort flag,
 // so one stalled role cannot leave the others spinning.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          long long limit_cycles = kWaitCycles) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait_sleep(a, parity, kSuspendNs)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit_cycles) {
       *abort_flag = 1;
       atomicOr(&g_vf_error, kErrWaitTimeout);
       return false;

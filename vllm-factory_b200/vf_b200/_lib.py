@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "vf_last_error",
     "vf_device_error",
     "vf_abi_version",
+    "vf_selftest_wait_timeout",
 )
 
 
@@ -126,6 +127,8 @@ def load() -> ctypes.CDLL:
         lib.vf_device_error.restype = ctypes.c_int
         lib.vf_abi_version.argtypes = []
         lib.vf_abi_version.restype = ctypes.c_int
+        lib.vf_selftest_wait_timeout.argtypes = [ctypes.c_int64, ctypes.c_void_p]
+        lib.vf_selftest_wait_timeout.restype = ctypes.c_int
         if lib.vf_abi_version() != ABI_VERSION:
             raise RuntimeError(f"{LIB_PATH}: ABI version {lib.vf_abi_version()} != {ABI_VERSION}")
         _lib = lib
@@ -152,6 +155,11 @@ def deberta_log_bucket(bucket_size: int, max_position: int, rmin: int, rmax: int
     buf = (ctypes.c_int32 * n)()
     check(load().vf_deberta_log_bucket(bucket_size, max_position, rmin, rmax, buf))
     return list(buf)
+
+
+def selftest_wait_timeout(limit_cycles: int = 2_000_000, stream: int = 0) -> None:
+    """Runs the bounded-wait self-test kernel (see include/vf_b200.h)."""
+    check(load().vf_selftest_wait_timeout(int(limit_cycles), ctypes.c_void_p(stream)))
 
 
 def device_error(clear: bool = True) -> int:
