@@ -239,6 +239,7 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
+        os.environ["NCCL_DEBUG"] = "WARN"   # rank 0's stdout carries only the JSON line
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=dev)
     import vf_b200

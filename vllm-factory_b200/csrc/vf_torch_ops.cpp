@@ -1,0 +1,204 @@
+// torch.ops.vf_b200.* — thin C++ op layer over the C ABI of libvf_b200.so.
+//
+// Tensors are read here (sizes, strides, data pointers, the current CUDA stream) and
+// passed as plain pointers/sizes to vf_rpb_attention_fwd / vf_deberta_attention_fwd; the
+// kernels, bucket tables and validation live behind the C ABI.  Only the output tensor is
+// allocated.  CPU tensors raise: there is no CPU implementation.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <cmath>
+#include <optional>
+#include <string>
+
+#include "vf_b200.h"
+
+namespace {
+
+vf_dtype_t dtype_code(const at::Tensor& t) {
+  switch (t.scalar_type()) {
+    case at::kFloat: return VF_DTYPE_F32;
+    case at::kHalf: return VF_DTYPE_F16;
+    case at::kBFloat16: return VF_DTYPE_BF16;
+    default: TORCH_CHECK(false, "vf_b200: unsupported dtype ", t.scalar_type());
+  }
+}
+
+vf_tensor4d_t view4(const at::Tensor& t) {
+  TORCH_CHECK(t.dim() == 4, "vf_b200: expected a 4-D tensor, got ", t.sizes());
+  vf_tensor4d_t d{};
+  d.data = t.data_ptr();
+  for (int i = 0; i < 4; ++i) {
+    d.size[i] = t.size(i);
+    d.stride[i] = t.stride(i);
+  }
+  return d;
+}
+
+// A layout TMA can describe: unit innermost stride, 16-byte aligned base and strides.
+at::Tensor tma_ready(const at::Tensor& t) {
+  const int64_t es = t.element_size();
+  bool ok = t.stride(3) == 1 && (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0;
+  for (int i = 0; i < 3 && ok; ++i) ok = t.stride(i) > 0 && (t.stride(i) * es) % 16 == 0;
+  return ok ? t : t.contiguous();
+}
+
+at::Tensor make_out(const at::Tensor& q) {
+  at::Tensor out = at::empty_like(q);
+  if (out.stride(3) != 1 || (out.stride(2) * out.element_size()) % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16) != 0)
+    out = at::empty(q.sizes(), q.options());
+  return out;
+}
+
+void require_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "vf_b200: ", name, " must be a CUDA tensor (no CPU implementation)");
+}
+
+void check_rc(int rc) {
+  TORCH_CHECK(rc == VF_OK, "vf_b200 error ", rc, ": ", vf_last_error());
+}
+
+at::Tensor rpb_attention(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
+                         const std::optional<at::Tensor>& rpb_table, int64_t num_buckets,
+                         int64_t max_distance, bool is_decoder,
+                         const std::optional<at::Tensor>& padding_mask, double dropout_p,
+                         double softmax_scale) {
+  require_cuda(q_in, "q");
+  require_cuda(k_in, "k");
+  require_cuda(v_in, "v");
+  TORCH_CHECK(q_in.scalar_type() == k_in.scalar_type() && q_in.scalar_type() == v_in.scalar_type(),
+              "vf_b200: q, k, v must share a dtype");
+  c10::cuda::CUDAGuard guard(q_in.device());
+  const at::Tensor q = tma_ready(q_in), k = tma_ready(k_in), v = tma_ready(v_in);
+  at::Tensor out = make_out(q);
+  vf_rpb_attention_args_t a{};
+  a.dtype = dtype_code(q);
+  a.q = view4(q);
+  a.k = view4(k);
+  a.v = view4(v);
+  a.out = view4(out);
+  if (rpb_table.has_value()) {
+    const at::Tensor& t = *rpb_table;
+    require_cuda(t, "rpb_table");
+    TORCH_CHECK(t.dim() == 2, "vf_b200: rpb_table must be [num_buckets, heads]");
+    a.rpb_table = t.data_ptr();
+    a.table_rows = t.size(0);
+    a.table_cols = t.size(1);
+    a.table_stride_row = t.stride(0);
+    a.table_stride_col = t.stride(1);
+    a.table_dtype = dtype_code(t);
+  }
+  a.num_buckets = static_cast<int32_t>(num_buckets);
+  a.max_distance = static_cast<int32_t>(max_distance);
+  a.is_decoder = is_decoder ? 1 : 0;
+  if (padding_mask.has_value()) {
+    require_cuda(*padding_mask, "padding_mask");
+    a.padding_mask = view4(*padding_mask);
+    a.mask_dtype = dtype_code(*padding_mask);
+  }
+  a.dropout_p = static_cast<float>(dropout_p);
+  a.softmax_scale = static_cast<float>(softmax_scale);
+  check_rc(vf_rpb_attention_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
+  return out;
+}
+
+at::Tensor deberta_attention(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
+                             const std::optional<at::Tensor>& seq_lengths,
+                             const std::optional<at::Tensor>& pos_key,
+                             const std::optional<at::Tensor>& pos_query, bool causal,
+                             std::optional<double> sm_scale, int64_t position_buckets,
+                             int64_t max_relative_distance, bool use_log_bucket) {
+  require_cuda(q_in, "q");
+  require_cuda(k_in, "k");
+  require_cuda(v_in, "v");
+  TORCH_CHECK(q_in.scalar_type() == k_in.scalar_type() && q_in.scalar_type() == v_in.scalar_type(),
+              "vf_b200: q, k, v must share a dtype");
+  c10::cuda::CUDAGuard guard(q_in.device());
+  const at::Tensor q = tma_ready(q_in), k = tma_ready(k_in), v = tma_ready(v_in);
+  at::Tensor out = make_out(q);
+  vf_deberta_attention_args_t a{};
+  a.dtype = dtype_code(q);
+  a.q = view4(q);
+  a.k = view4(k);
+  a.v = view4(v);
+  a.out = view4(out);
+  at::Tensor lens;
+  if (seq_lengths.has_value()) {
+    require_cuda(*seq_lengths, "seq_lengths");
+    lens = *seq_lengths;
+    if (lens.scalar_type() != at::kInt || !lens.is_contiguous()) lens = lens.to(at::kInt).contiguous();
+    TORCH_CHECK(lens.numel() == q.size(0), "vf_b200: seq_lengths must have one entry per batch row");
+    a.seq_lengths = lens.data_ptr<int32_t>();
+  }
+  if (pos_key.has_value()) {
+    require_cuda(*pos_key, "pos_key");
+    TORCH_CHECK(pos_key->scalar_type() == q.scalar_type(), "vf_b200: pos_key must have the dtype of q");
+    a.pos_key = view4(*pos_key);
+  }
+  if (pos_query.has_value()) {
+    require_cuda(*pos_query, "pos_query");
+    TORCH_CHECK(pos_query->scalar_type() == q.scalar_type(), "vf_b200: pos_query must have the dtype of q");
+    a.pos_query = view4(*pos_query);
+  }
+  a.causal = causal ? 1 : 0;
+  a.has_sm_scale = sm_scale.has_value() ? 1 : 0;
+  a.sm_scale = sm_scale.has_value() ? static_cast<float>(*sm_scale) : 0.f;
+  a.position_buckets = static_cast<int32_t>(position_buckets);
+  a.max_relative_distance = static_cast<int32_t>(max_relative_distance);
+  a.use_log_bucket = use_log_bucket ? 1 : 0;
+  check_rc(vf_deberta_attention_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
+  return out;
+}
+
+// Shape functions for tracing (torch.compile / fake tensors).
+at::Tensor rpb_attention_meta(const at::Tensor& q, const at::Tensor&, const at::Tensor&,
+                              const std::optional<at::Tensor>&, int64_t, int64_t, bool,
+                              const std::optional<at::Tensor>&, double, double) {
+  return at::empty_like(q);
+}
+at::Tensor deberta_attention_meta(const at::Tensor& q, const at::Tensor&, const at::Tensor&,
+                                  const std::optional<at::Tensor>&, const std::optional<at::Tensor>&,
+                                  const std::optional<at::Tensor>&, bool, std::optional<double>, int64_t,
+                                  int64_t, bool) {
+  return at::empty_like(q);
+}
+
+at::Tensor rpb_attention_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                             const std::optional<at::Tensor>&, int64_t, int64_t, bool,
+                             const std::optional<at::Tensor>&, double, double) {
+  TORCH_CHECK(false, "vf_b200: q, k, v must be CUDA tensors (no CPU implementation)");
+}
+at::Tensor deberta_attention_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                 const std::optional<at::Tensor>&, const std::optional<at::Tensor>&,
+                                 const std::optional<at::Tensor>&, bool, std::optional<double>, int64_t,
+                                 int64_t, bool) {
+  TORCH_CHECK(false, "vf_b200: q, k, v must be CUDA tensors (no CPU implementation)");
+}
+
+}  // namespace
+
+TORCH_LIBRARY(vf_b200, m) {
+  m.def("rpb_attention(Tensor q, Tensor k, Tensor v, Tensor? rpb_table, int num_buckets, int max_distance, "
+        "bool is_decoder, Tensor? padding_mask, float dropout_p, float softmax_scale) -> Tensor");
+  m.def("deberta_attention(Tensor q, Tensor k, Tensor v, Tensor? seq_lengths, Tensor? pos_key, "
+        "Tensor? pos_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "
+        "bool use_log_bucket) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(vf_b200, CUDA, m) {
+  m.impl("rpb_attention", &rpb_attention);
+  m.impl("deberta_attention", &deberta_attention);
+}
+
+TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
+  m.impl("rpb_attention", &rpb_attention_cpu);
+  m.impl("deberta_attention", &deberta_attention_cpu);
+}
+
+TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
+  m.impl("rpb_attention", &rpb_attention_meta);
+  m.impl("deberta_attention", &deberta_attention_meta);
+}

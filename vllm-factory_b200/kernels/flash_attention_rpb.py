@@ -15,7 +15,7 @@ from typing import Optional
 
 import torch
 
-import vf_b200  # noqa: F401  (registers torch.ops.vf_b200)
+import vf_b200.ops  # noqa: F401  (loads the kernels and registers torch.ops.vf_b200)
 
 
 def flash_attention_rpb_final(

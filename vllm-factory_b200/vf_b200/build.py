@@ -16,8 +16,11 @@ PKG_DIR = Path(__file__).resolve().parent
 CSRC = PKG_DIR.parent / "csrc"
 INCLUDE = PKG_DIR.parent.parent / "include"
 LIB_PATH = PKG_DIR / "libvf_b200.so"
+TORCH_LIB_PATH = PKG_DIR / "libvf_b200_torch.so"
 SOURCES = [CSRC / "vf_attention.cu"]
 DEPS = SOURCES + [CSRC / "vf_ptx.cuh", INCLUDE / "vf_b200.h"]
+TORCH_SOURCES = [CSRC / "vf_torch_ops.cpp"]
+TORCH_DEPS = TORCH_SOURCES + [INCLUDE / "vf_b200.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -34,16 +37,52 @@ def nvcc_path() -> str:
     return cand
 
 
-def is_stale() -> bool:
-    if not LIB_PATH.exists():
+def _stale(target: Path, deps) -> bool:
+    if not target.exists():
         return True
-    t = LIB_PATH.stat().st_mtime
-    return any(p.stat().st_mtime > t for p in DEPS if p.exists())
+    t = target.stat().st_mtime
+    return any(p.stat().st_mtime > t for p in deps if p.exists())
+
+
+def is_stale() -> bool:
+    return _stale(LIB_PATH, DEPS) or _stale(TORCH_LIB_PATH, TORCH_DEPS + [LIB_PATH])
+
+
+def build_torch_ops(force: bool = False, verbose: bool = False) -> Path:
+    """Compiles the torch op layer (csrc/vf_torch_ops.cpp) against torch's headers and the
+    C ABI library; the result is loaded with torch.ops.load_library."""
+    if not force and not _stale(TORCH_LIB_PATH, TORCH_DEPS + [LIB_PATH]):
+        return TORCH_LIB_PATH
+    import torch
+    from torch.utils import cpp_extension as ce
+    cxx = os.environ.get("CXX", shutil.which("g++") or "c++")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    incs = [f"-I{p}" for p in ce.include_paths(device_type="cuda")] + [f"-I{INCLUDE}"]
+    libdirs = ce.library_paths(device_type="cuda")
+    tmp = TORCH_LIB_PATH.with_suffix(".so.tmp")
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           *incs, *map(str, TORCH_SOURCES), "-o", str(tmp),
+           *[f"-L{d}" for d in libdirs], "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda",
+           f"-L{PKG_DIR}", "-lvf_b200", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"torch op layer build failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, TORCH_LIB_PATH)
+    return TORCH_LIB_PATH
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
-    """Compiles the library if it is missing or older than its sources; returns its path."""
-    if not force and not is_stale():
+    """Compiles whatever is missing or older than its sources; returns the kernel library."""
+    build_kernels(force=force, verbose=verbose)
+    build_torch_ops(force=force, verbose=verbose)
+    return LIB_PATH
+
+
+def build_kernels(force: bool = False, verbose: bool = False) -> Path:
+    """nvcc: the sm_100a kernels and the C ABI -> libvf_b200.so."""
+    if not force and not _stale(LIB_PATH, DEPS):
         return LIB_PATH
     tmp = LIB_PATH.with_suffix(".so.tmp")
     cmd = [nvcc_path(), *NVCC_FLAGS, "-I", str(INCLUDE), "-o", str(tmp), *map(str, SOURCES)]
