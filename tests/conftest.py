@@ -22,3 +22,20 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _device_error_word_clean(request):
+    """Every GPU test must leave the kernels' device error word at zero: a bounded wait
+    that ran out (a lost arrival, a pipeline mismatch) is a failure even when the
+    output happens to be right."""
+    yield
+    if "gpu" not in request.keywords:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    import vf_b200
+    torch.cuda.synchronize()
+    word = vf_b200.device_error(clear=True)
+    assert word == 0, f"device error word {word:#x} after {request.node.name}"

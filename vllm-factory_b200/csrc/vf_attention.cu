@@ -6,25 +6,28 @@
 //   * kDeberta — kernels/flash_deberta_attention.py:145-299 (_flash_deberta_fwd_kernel):
 //                s = sm_scale * (q.k + pos_key[m, idx(m - n)] + pos_query[n, idx(m - n)])
 //
-// CTA = 256 query rows of one (batch, head) as two 128-row tiles, keys in 128-row tiles.
+// Persistent launch: one CTA per SM walks a list of work units; a unit is 256 query rows
+// of one (batch, head) as two 128-row tiles, against that batch's live 128-key tiles.
 // Warp roles (384 threads = 3 warpgroups):
 //   warps 0-3  softmax group 0 (query tile 0), one thread per query row
 //   warps 4-7  softmax group 1 (query tile 1)
-//   warp  8    TMA producer (Q once, then a 3-stage K/V ring)
+//   warp  8    TMA producer (Q per unit, double-buffered; a 3-stage K/V ring across units)
 //   warp  9    UMMA issuer (one elected lane) + TMEM allocation
-//   warps 10-11 idle
-// Launched at 168 registers/thread; after the prologue the producer warpgroup drops to
-// 56 and the softmax warpgroups rise to 224 (2*128*224 + 128*56 = 384*168).
+//   warp  10   unit preparation (schedule, live key span, per-head bias table), one unit ahead
+//   warp  11   idle
+// Register split after the prologue: see kRegsSoftmax / kRegsProducer.
 // TMEM (512 columns, fp32): per query tile g, S at 256g, P (bf16 pairs) at 256g+128,
 // O at 256g+192.  S = Q K^T and O += P V run on tcgen05.mma (kind::f16, fp32 accumulate);
 // softmax threads read S with tcgen05.ld, write P back with tcgen05.st, and the PV MMA
-// takes P straight from TMEM.  All waits are bounded (see vf_ptx.cuh).
+// takes P straight from TMEM.  O leaves through a shared-memory staging tile and a TMA
+// bulk store.  All waits are bounded (see vf_ptx.cuh).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -32,6 +35,7 @@
 #include <mutex>
 #include <string>
 #include <tuple>
+#include <type_traits>
 #include <vector>
 
 #include "vf_ptx.cuh"
@@ -40,29 +44,46 @@
 namespace vf {
 
 constexpr int kBM = 128;          // query rows per tile
-constexpr int kNQ = 2;            // query tiles per CTA
+constexpr int kNQ = 2;            // query tiles per work unit (softmax groups per CTA)
 constexpr int kBN = 128;          // keys per tile
 constexpr int kHeadDim = 64;
 constexpr int kStages = 3;        // K/V ring depth
 constexpr int kTileBytes = kBM * kHeadDim * 2;   // 16 KB for a 128 x 64 16-bit tile
-constexpr int kThreads = 384;
-constexpr uint32_t kRegsSoftmax = 224;
-constexpr uint32_t kRegsProducer = 56;
-constexpr int kLoadWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr uint32_t kTmemCols = 512;
-constexpr int kMaxRel = 2048;               // relative-position table radius limit
+constexpr int kSoftmaxWarps = 4 * kNQ;
+constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
+constexpr int kThreads = kSoftmaxThreads + 128;
+// Launched at 168 registers/thread; after the prologue the producer warpgroup drops to
+// 88 and the softmax warpgroups rise to 208 (2*128*208 + 128*88 = 384*168).  The softmax
+// path fits in 208 without spills; the producer roles (loader, UMMA issuer, unit
+// preparation) are latency-critical and get the rest.
+constexpr uint32_t kRegsSoftmax = 208;
+constexpr uint32_t kRegsProducer = 88;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsProducer == 384 * 168, "setmaxnreg split must use the launch budget");
+constexpr int kLoadWarp = kSoftmaxWarps;
+constexpr int kMmaWarp = kSoftmaxWarps + 1;
+constexpr int kPrepWarp = kSoftmaxWarps + 2;
+constexpr uint32_t kTmemCols = 256 * kNQ;
+constexpr int kMaxRel = 1024;               // relative-position table radius limit
 constexpr int kMaxLut = 2 * kMaxRel + 1;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kDeadMask = -1.0e4f;        // additive mask at/below this kills a key
 constexpr float kMaskFloor = -1.0e30f;      // masks are clamped here before scaling
-constexpr float kRescaleThreshold = 8.0f;   // lazy O rescale (log2 units)
+#ifndef VF_RESCALE_BF16
+#define VF_RESCALE_BF16 32.0f
+#endif
 constexpr int kPolyEvery = 3;               // every 3rd exponential pair on the FMA pipe
+#ifndef VF_BIAS_CHUNK
+#define VF_BIAS_CHUNK 16
+#endif
+// Bias-table loads are issued kBiasChunk column pairs at a time: the compiler may not
+// hoist more of them ahead of their use (each holds registers next to the 128 scores).
+constexpr int kBiasChunk = VF_BIAS_CHUNK;
+__device__ __forceinline__ void smem_load_fence() { asm volatile("" ::: "memory"); }
 
 enum Variant : int { kT5 = 0, kDeberta = 1 };
 
 struct __align__(64) KParams {
-  CUtensorMap tm_q, tm_k, tm_v;
+  CUtensorMap tm_q, tm_k, tm_v, tm_o;
   void* out;
   long long o_sb, o_sh, o_sm;
   int B, H, M, N;
@@ -87,29 +108,39 @@ struct __align__(64) KParams {
   short lut[kMaxLut];    // T5: bucket of r = n - m;  DeBERTa: idx of r = m - n
 };
 
-// Shared-memory carve-up (offsets from a 1024-aligned base).
+// Shared-memory carve-up (offsets from a 1024-aligned base).  Q is double-buffered by
+// unit, K/V by key tile, the T5 bias table by unit; each group stages its O tile for
+// the bulk store.
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kNQ * kTileBytes;
+constexpr int kOffK = kOffQ + 2 * kNQ * kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
+constexpr int kOffOStage = kOffV + kStages * kTileBytes;
 constexpr int kRPad = 160;                  // bias-table padding: a warp's window never clamps
-constexpr int kOffKBias = kOffV + kStages * kTileBytes;
+constexpr int kRBiasLen = (kMaxLut + 2 * kRPad + 3) & ~3;
+constexpr int kOffKBias = kOffOStage + kNQ * kTileBytes;
 constexpr int kOffKZero = kOffKBias + kStages * kBN * 4;         // per stage: key mask all zero
 constexpr int kOffRBias = kOffKZero + 16;
-constexpr int kOffLut = kOffRBias + (kMaxLut + 2 * kRPad) * 4 + 12;   // keep 16-byte alignment
-constexpr int kOffBar = (kOffLut + kMaxLut * 2 + 15 + 64) & ~15;
-// barriers: q_full, s_full[2], p_full[2], s_consumed[2], pv_done[2], k_full[3], v_full[3],
-// kv_empty[3], drain
-constexpr int kNumBars = 1 + 2 + 2 + 2 + 2 + 3 * kStages + 1;
+constexpr int kOffLut = kOffRBias + 2 * kRBiasLen * 4;
+constexpr int kOffBar = (kOffLut + kMaxLut * 2 + 15) & ~15;
+// barriers: q_full[2], q_empty[2], s_full[2], p_full[2], s_consumed[2], pv_done[2],
+// info_full[2], info_empty[2], stage_free[2], stage_full[2], k_full/v_full/kv_empty[kStages],
+// drain
+constexpr int kNumBars = 20 + 3 * kStages + 1;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
-constexpr int kSmemBytes = kOffMisc + 64;
+constexpr int kOffInfo = kOffMisc + 16;
+constexpr int kMaxLptPairs = 1024;          // (batch, query block) pairs ordered by cost
+constexpr int kMaxLptSamples = 2048;        // T5 mask samples (batch x key tile) for the costs
+constexpr int kOffOrder = kOffInfo + 2 * 64;                      // uint16_t[kMaxLptPairs]
+constexpr int kOffCost = kOffOrder + 2 * kMaxLptPairs;            // uint8_t[kMaxLptPairs]
+constexpr int kOffLive = kOffCost + kMaxLptPairs;                 // uint8_t[kMaxLptSamples]
+constexpr int kSmemBytes = kOffLive + kMaxLptSamples;
 constexpr int kSmemAlloc = kSmemBytes + 1024;
 
 struct SmemMisc {
   uint32_t tmem_base;
   int abort_flag;
-  int live_lo;
-  int live_hi;
 };
+static_assert(kSmemAlloc <= 227 * 1024, "shared memory over the per-CTA limit");
 
 template <typename T> __device__ __forceinline__ float to_f(T v);
 template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
@@ -125,6 +156,11 @@ template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float 
 template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) { return pack_bf16x2(lo, hi); }
 template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) { return pack_f16x2(lo, hi); }
 
+// Lazy-rescale threshold (log2 units): P = 2^(x - m_run) stays below 2^(threshold + 1).
+// bf16 has the fp32 exponent range; fp16 P must stay well inside 65504.
+template <typename T> struct RescaleThreshold;
+template <> struct RescaleThreshold<__nv_bfloat16> { static constexpr float value = VF_RESCALE_BF16; };
+template <> struct RescaleThreshold<__half> { static constexpr float value = 8.0f; };
 template <typename T> struct AbFormat;
 template <> struct AbFormat<__nv_bfloat16> { static constexpr uint32_t value = 1u; };
 template <> struct AbFormat<__half> { static constexpr uint32_t value = 0u; };
@@ -141,50 +177,198 @@ __device__ void zero_rows(const KParams& p, int b, int h, int r0, int r1, int ti
   }
 }
 
+template <typename M> __device__ __forceinline__ float ld_f(const M* p) { return to_f<M>(p[0]); }
+template <> __device__ __forceinline__ float ld_f<float>(const float* p) { return __ldg(p); }
+
+// Live span of one mask row (additive mask > kDeadMask), per lane; eight loads in flight.
+template <typename M>
+__device__ __forceinline__ void live_span(const void* mask, long long base, long long stride, int N, int lane,
+                                          int& lo, int& hi) {
+  const M* row = reinterpret_cast<const M*>(mask) + base;
+  for (int n0 = 0; n0 < N; n0 += 8 * 32) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int n = n0 + lane + 32 * j;
+      v[j] = n < N ? ld_f<M>(row + n * stride) : -INFINITY;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (v[j] > kDeadMask) {
+        const int n = n0 + lane + 32 * j;
+        lo = min(lo, n);
+        hi = max(hi, n);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float half_bits_to_f(uint32_t u, bool is_bf16) {
+  return is_bf16 ? __uint_as_float(u << 16) : __half2float(__ushort_as_half(static_cast<unsigned short>(u)));
+}
+
+// Same for a contiguous 16-bit mask row starting on a 16-byte boundary: 8 values per
+// 16-byte load, four loads in flight per lane.
+__device__ __forceinline__ void live_span_vec16(const void* mask, long long base, int N, bool is_bf16, int lane,
+                                                int& lo, int& hi) {
+  const uint16_t* row = reinterpret_cast<const uint16_t*>(mask) + base;
+  const uint4* vrow = reinterpret_cast<const uint4*>(row);
+  const int nvec = N / 8;
+  for (int c0 = 0; c0 < nvec; c0 += 4 * 32) {
+    uint4 w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = c0 + lane + 32 * j;
+      w[j] = c < nvec ? __ldg(vrow + c) : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = c0 + lane + 32 * j;
+      if (c >= nvec) continue;
+      const uint32_t ws[4] = {w[j].x, w[j].y, w[j].z, w[j].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int n = 8 * c + 2 * q;
+        if (half_bits_to_f(ws[q] & 0xffffu, is_bf16) > kDeadMask) { lo = min(lo, n); hi = max(hi, n); }
+        if (half_bits_to_f(ws[q] >> 16, is_bf16) > kDeadMask) { lo = min(lo, n + 1); hi = max(hi, n + 1); }
+      }
+    }
+  }
+  for (int n = 8 * nvec + lane; n < N; n += 32) {
+    if (half_bits_to_f(row[n], is_bf16) > kDeadMask) { lo = min(lo, n); hi = max(hi, n); }
+  }
+}
+
+// rbias[r + R + kRPad] = table[bucket(r), h] * log2(e) for r in [-R - kRPad, R + kRPad];
+// beyond +-R the bucket is saturated, so the padding repeats the end values.
+template <typename M>
+__device__ __forceinline__ void fill_bias(const KParams& p, const short* lut_s, float* rb, int h, int lane) {
+  const M* tab = reinterpret_cast<const M*>(p.table) + (long long)h * p.tb_scol;
+  const int n = 2 * (p.rel_R + kRPad) + 1;
+  for (int e0 = 0; e0 < n; e0 += 8 * 32) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = e0 + lane + 32 * j;
+      const int rc = min(max(e - kRPad, 0), 2 * p.rel_R);
+      v[j] = e < n ? ld_f<M>(tab + (long long)lut_s[rc] * p.tb_srow) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = e0 + lane + 32 * j;
+      if (e < n) rb[e] = v[j] * kLog2e;
+    }
+  }
+}
+
+// One work unit: kNQ * kBM query rows of one (batch, head) against that batch's live key
+// tiles.  Units are ordered by estimated cost, longest first, and dealt to the CTAs in
+// snake order (c, 2G-1-c, 2G+c, ...), so every CTA ends up with a similar amount of work.
+struct UnitInfo {
+  int valid;             // 0: the CTA's work list has ended
+  int b, h, q0;
+  int t_begin, nkv;      // key tiles [t_begin, t_begin + nkv)
+  int klen, qlen;        // valid keys / rows (DeBERTa seq_len; T5: N and M)
+};
+static_assert(sizeof(UnitInfo) <= 64, "unit slot");
+
+// Whether the CTA orders its units by cost: the (batch, query block) pairs and, for a
+// T5 mask, the (batch, key tile) mask samples must fit the shared-memory tables.
+template <int kVariant>
+__device__ __forceinline__ bool lpt_enabled(const KParams& p) {
+  const int nqb = (p.M + kNQ * kBM - 1) / (kNQ * kBM);
+  const int ntile = (p.N + kBN - 1) / kBN;
+  if ((long long)p.B * nqb > kMaxLptPairs) return false;
+  if (kVariant == kT5 && p.mask != nullptr && (long long)p.B * ntile > kMaxLptSamples) return false;
+  return true;
+}
+
+// Estimated key tiles of the units of (batch b, query block qb): seq_len for DeBERTa, the
+// mask sampled at each tile's first key for T5 (`live`, exact for contiguous padding;
+// only the schedule depends on it), trimmed by causality.
+template <int kVariant>
+__device__ int pair_cost(const KParams& p, const uint8_t* live, int b, int qb) {
+  const int q0 = qb * (kNQ * kBM);
+  int klen = p.N, qlen = p.M;
+  if (kVariant == kDeberta && p.seq_lengths != nullptr) {
+    const int L = __ldg(p.seq_lengths + b);
+    klen = min(max(L, 0), p.N);
+    qlen = min(max(L, 0), p.M);
+  }
+  if (kVariant == kDeberta && q0 >= qlen) return 0;
+  int t_end = (klen + kBN - 1) / kBN;
+  if (p.causal) {
+    const int last_key = min(q0 + kNQ * kBM, p.M) - 1 + p.p_seq;
+    t_end = min(t_end, last_key < 0 ? 0 : last_key / kBN + 1);
+  }
+  int n = t_end;
+  if (kVariant == kT5 && p.mask != nullptr) {
+    const int ntile = (p.N + kBN - 1) / kBN;
+    n = 0;
+    for (int kt = 0; kt < t_end; ++kt) n += live[b * ntile + kt];
+    if (n == 0) n = t_end;   // every key dead: every tile is visited
+  }
+  return n;
+}
+
+// Unit i of this CTA.  `order` lists the (batch, query block) pairs by cost, longest
+// first (nullptr: natural order); each pair stands for H units, one per head.
+__device__ __forceinline__ bool unit_coords(const KParams& p, const uint16_t* order, int i, int& b, int& h,
+                                            int& q0) {
+  const int nqb = (p.M + kNQ * kBM - 1) / (kNQ * kBM);
+  const long long G = gridDim.x;
+  const long long k = (long long)i * G + ((i & 1) ? G - 1 - blockIdx.x : blockIdx.x);
+  if (k >= (long long)p.H * nqb * p.B) return false;
+  const int pair_rank = static_cast<int>(k / p.H);
+  h = static_cast<int>(k % p.H);
+  const int pair = order != nullptr ? order[pair_rank] : pair_rank;
+  b = pair / nqb;
+  q0 = (pair % nqb) * (kNQ * kBM);
+  return true;
+}
+
 template <int kVariant, typename T>
 __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ KParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* kbias = reinterpret_cast<float*>(smem + kOffKBias);
-  float* rbias = reinterpret_cast<float*>(smem + kOffRBias);   // index r + R + kRPad
+  float* rbias_buf = reinterpret_cast<float*>(smem + kOffRBias);   // [2][kRBiasLen], index r + R + kRPad
   int* kzero = reinterpret_cast<int*>(smem + kOffKZero);
   short* lut_s = reinterpret_cast<short*>(smem + kOffLut);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars + 0;
-  uint64_t* s_full = bars + 1;        // [2] S = Q K^T of the tile is in TMEM
-  uint64_t* p_full = bars + 3;        // [2] P of the tile is in TMEM
-  uint64_t* s_consumed = bars + 5;    // [2] softmax has read S into registers
-  uint64_t* pv_done = bars + 7;       // [2] O += P V of the tile has completed
-  uint64_t* k_full = bars + 9;        // [kStages]
+  uint64_t* q_full = bars + 0;        // [2] Q tiles of a unit are in shared memory
+  uint64_t* q_empty = bars + 2;       // [2] every QK reading that Q buffer has completed
+  uint64_t* s_full = bars + 4;        // [2] S = Q K^T of the tile is in TMEM
+  uint64_t* p_full = bars + 6;        // [2] P of the tile is in TMEM
+  uint64_t* s_consumed = bars + 8;    // [2] softmax has read S into registers
+  uint64_t* pv_done = bars + 10;      // [2] O += P V of the tile has completed
+  uint64_t* info_full = bars + 12;    // [2] unit description and bias table published
+  uint64_t* info_empty = bars + 14;   // [2] every role is done with that unit slot
+  uint64_t* stage_free = bars + 16;   // [2] the group's previous O store has read its staging tile
+  uint64_t* stage_full = bars + 18;   // [2] the group's O rows are staged for the store
+  uint64_t* k_full = bars + 20;       // [kStages]
   uint64_t* v_full = k_full + kStages;
   uint64_t* kv_empty = v_full + kStages;
   uint64_t* drain = kv_empty + kStages;
   SmemMisc* misc = reinterpret_cast<SmemMisc*>(smem + kOffMisc);
+  UnitInfo* info = reinterpret_cast<UnitInfo*>(smem + kOffInfo);   // [2]
   volatile int* abort_flag = &misc->abort_flag;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
-  const int q0 = blockIdx.x * (kNQ * kBM);
   const int R = p.rel_R;
-
-  // Valid keys / rows.  DeBERTa: seq_lengths (right padding); rows past it are written 0.
-  int klen = p.N, qlen = p.M;
-  if (kVariant == kDeberta && p.seq_lengths != nullptr) {
-    const int L = p.seq_lengths[b];
-    klen = min(max(L, 0), p.N);
-    qlen = min(max(L, 0), p.M);
-  }
-  if (kVariant == kDeberta && q0 >= qlen) {
-    zero_rows<T>(p, b, h, q0, min(q0 + kNQ * kBM, p.M), tid, kThreads);
-    return;
-  }
-
   const bool has_mask = (kVariant == kT5) && (p.mask != nullptr);
+
   if (tid == 0) {
-    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+      mbar_init(&info_full[s], 32);
+      mbar_init(&info_empty[s], kSoftmaxThreads + 2);
+      mbar_init(&stage_free[s], 1);
+      mbar_init(&stage_full[s], kBM);
+    }
     for (int g = 0; g < kNQ; ++g) {
       mbar_init(&s_full[g], 1);
       mbar_init(&p_full[g], kBM);
@@ -198,13 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     }
     mbar_init(drain, 1);
     misc->abort_flag = 0;
-    misc->live_lo = 0x7fffffff;
-    misc->live_hi = -1;
     fence_mbar_init();
-    // Q does not depend on the key range: start its copy before the prologue work.
-    mbar_arrive_expect_tx(q_full, kNQ * kTileBytes);
-    for (int g = 0; g < kNQ; ++g)
-      tma_load_4d(smem + kOffQ + g * kTileBytes, &p.tm_q, q_full, 0, q0 + g * kBM, h, b);
   }
   if (warp == kMmaWarp) {
     tmem_alloc(&misc->tmem_base, kTmemCols);
@@ -214,106 +392,207 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     tma_prefetch_desc(&p.tm_q);
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
+    tma_prefetch_desc(&p.tm_o);
   }
-  // Relative-position tables into shared memory.
+  // Relative-position lookup table (the same for every unit).
   for (int i = tid; i <= 2 * R; i += kThreads) lut_s[i] = p.lut[i];
-  if (kVariant == kT5) {
-    // rbias[r + R + kRPad] = table[bucket(r), h] * log2(e) for r in [-R - kRPad, R + kRPad];
-    // beyond +-R the bucket is saturated, so the padding repeats the end values.
-    for (int i = tid; i <= 2 * (R + kRPad); i += kThreads) {
-      const int rc = min(max(i - kRPad, 0), 2 * R);
-      const short v = p.lut[rc];
-      rbias[i] = (p.table != nullptr)
-                     ? load_any(p.table, (long long)v * p.tb_srow + (long long)h * p.tb_scol, p.table_dtype) * kLog2e
-                     : 0.f;
+  // T5 mask samples for the unit costs (one load per thread for typical sizes).
+  if (has_mask && lpt_enabled<kVariant>(p)) {
+    uint8_t* live = smem + kOffLive;
+    const int ntile = (p.N + kBN - 1) / kBN;
+    for (int it = tid; it < p.B * ntile; it += kThreads) {
+      const int b = it / ntile, kt = it % ntile;
+      live[it] = load_any(p.mask, b * p.mk_sb + (long long)kt * kBN * p.mk_sn, p.mask_dtype) > kDeadMask ? 1 : 0;
     }
-  }
-  // T5: the span of keys whose mask is alive bounds the key tiles worth visiting.
-  if (has_mask) {
-    int lo = 0x7fffffff, hi = -1;
-    for (int n = tid; n < p.N; n += kThreads) {
-      const float mv = load_any(p.mask, b * p.mk_sb + h * p.mk_sh + n * p.mk_sn, p.mask_dtype);
-      if (mv > kDeadMask) { lo = min(lo, n); hi = max(hi, n); }
-    }
-    if (hi >= 0) { atomicMin(&misc->live_lo, lo); atomicMax(&misc->live_hi, hi); }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc->tmem_base;
 
-  // Key-tile range [t_begin, t_end).
-  int t_begin = 0, t_end = (klen + kBN - 1) / kBN;
-  if (has_mask && misc->live_hi >= 0) {
-    t_begin = misc->live_lo / kBN;
-    t_end = misc->live_hi / kBN + 1;
-  }
-  if (p.causal) {
-    // Keys a row may see: n <= m + p_seq, m < q0 + 256.
-    const int last_key = min(q0 + kNQ * kBM, p.M) - 1 + p.p_seq;
-    t_end = min(t_end, last_key < 0 ? 0 : last_key / kBN + 1);
-  }
-  const int nkv = max(t_end - t_begin, 0);
-
-  if (warp >= 8) {
+  if (warp >= kSoftmaxWarps) {
   reg_dealloc<kRegsProducer>();
-  if (warp == kLoadWarp) {
-    // ------------------------------------------------------------ TMA producer
-    int issued = 0;
-    for (int t = 0; t < nkv; ++t) {
-      const int s = t % kStages;
-      const int round = t / kStages;
-      if (round > 0) {
-        const bool ok = mbar_wait(&kv_empty[s], (round - 1) & 1, abort_flag);
+  if (warp == kPrepWarp) {
+    // ------------------------------------------------------------ unit preparation
+    // Describes unit i in slot i & 1: live key range (mask scan), and for T5 the bias
+    // table of the unit's head.  Runs one unit ahead of the other roles.
+    uint16_t* order = reinterpret_cast<uint16_t*>(smem + kOffOrder);
+    uint8_t* cost = smem + kOffCost;
+    const int nqb = (p.M + kNQ * kBM - 1) / (kNQ * kBM);
+    const bool lpt = lpt_enabled<kVariant>(p);
+    if (lpt) {
+      // Stable counting sort of the pairs by estimated cost, descending.
+      const int P = p.B * nqb;
+      const uint8_t* live = smem + kOffLive;
+      int maxc = 0;
+      for (int pi = lane; pi < P; pi += 32) {
+        const int c = min(pair_cost<kVariant>(p, live, pi / nqb, pi % nqb), 255);
+        cost[pi] = static_cast<uint8_t>(c);
+        maxc = max(maxc, c);
+      }
+      maxc = __reduce_max_sync(0xffffffffu, maxc);
+      __syncwarp();
+      int pos = 0;
+      for (int c = maxc; c >= 0; --c) {
+        for (int base = 0; base < P; base += 32) {
+          const int pi = base + lane;
+          const bool match = pi < P && cost[pi] == c;
+          const uint32_t ballot = __ballot_sync(0xffffffffu, match);
+          if (match) order[pos + __popc(ballot & ((1u << lane) - 1u))] = static_cast<uint16_t>(pi);
+          pos += __popc(ballot);
+        }
+      }
+      __syncwarp();
+    }
+    for (int i = 0;; ++i) {
+      const int slot = i & 1;
+      if (i >= 2) {
+        const bool ok = mbar_wait(&info_empty[slot], ((i - 2) >> 1) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) break;
       }
-      const int k0 = (t_begin + t) * kBN;
-      issued = t + 1;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&k_full[s], kTileBytes);
-        tma_load_4d(smem + kOffK + s * kTileBytes, &p.tm_k, &k_full[s], 0, k0, h, b);
-        mbar_arrive_expect_tx(&v_full[s], kTileBytes);
-        tma_load_4d(smem + kOffV + s * kTileBytes, &p.tm_v, &v_full[s], 0, k0, h, b);
-      }
-      if (has_mask) {
-        bool zero = true;
-#pragma unroll
-        for (int i = 0; i < kBN / 32; ++i) {
-          const int c = lane + 32 * i;
-          const int n = k0 + c;
-          float mv = 0.f;
-          if (n < p.N) mv = load_any(p.mask, b * p.mk_sb + h * p.mk_sh + n * p.mk_sn, p.mask_dtype);
-          zero = zero && (mv == 0.f);
-          kbias[s * kBN + c] = fmaxf(mv, kMaskFloor) * kLog2e;
+      int b = 0, h = 0, q0 = 0;
+      const bool valid = unit_coords(p, lpt ? order : nullptr, i, b, h, q0);
+      int klen = p.N, qlen = p.M, t_begin = 0, t_end = 0;
+      if (valid) {
+        if (kVariant == kDeberta && p.seq_lengths != nullptr) {
+          const int L = __ldg(p.seq_lengths + b);
+          klen = min(max(L, 0), p.N);
+          qlen = min(max(L, 0), p.M);
         }
-        zero = __all_sync(0xffffffffu, zero);
-        if (lane == 0) kzero[s] = zero ? 1 : 0;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&k_full[s]);
+        t_end = (klen + kBN - 1) / kBN;
+        if (has_mask) {
+          // The span of keys whose mask is alive bounds the key tiles worth visiting.
+          int lo = 0x7fffffff, hi = -1;
+          const long long base = b * p.mk_sb + h * p.mk_sh;
+          const bool vec16 = p.mask_dtype != VF_DTYPE_F32 && p.mk_sn == 1 &&
+                             ((reinterpret_cast<uintptr_t>(p.mask) + base * 2) & 15) == 0;
+          if (vec16)
+            live_span_vec16(p.mask, base, p.N, p.mask_dtype == VF_DTYPE_BF16, lane, lo, hi);
+          else if (p.mask_dtype == VF_DTYPE_BF16)
+            live_span<__nv_bfloat16>(p.mask, base, p.mk_sn, p.N, lane, lo, hi);
+          else if (p.mask_dtype == VF_DTYPE_F16)
+            live_span<__half>(p.mask, base, p.mk_sn, p.N, lane, lo, hi);
+          else
+            live_span<float>(p.mask, base, p.mk_sn, p.N, lane, lo, hi);
+          lo = __reduce_min_sync(0xffffffffu, lo);
+          hi = __reduce_max_sync(0xffffffffu, hi);
+          if (hi >= 0) { t_begin = lo / kBN; t_end = hi / kBN + 1; }   // else every key is dead: visit all
+        }
+        if (p.causal) {
+          // Keys a row may see: n <= m + p_seq, m < q0 + kNQ * kBM.
+          const int last_key = min(q0 + kNQ * kBM, p.M) - 1 + p.p_seq;
+          t_end = min(t_end, last_key < 0 ? 0 : last_key / kBN + 1);
+        }
+        if (kVariant == kDeberta && q0 >= qlen) t_end = t_begin;   // rows all padded: zeros only
+        if (kVariant == kT5) {
+          float* rb = rbias_buf + slot * kRBiasLen;
+          if (p.table == nullptr) {
+            for (int e = lane; e <= 2 * (R + kRPad); e += 32) rb[e] = 0.f;
+          } else if (p.table_dtype == VF_DTYPE_BF16) {
+            fill_bias<__nv_bfloat16>(p, lut_s, rb, h, lane);
+          } else if (p.table_dtype == VF_DTYPE_F16) {
+            fill_bias<__half>(p, lut_s, rb, h, lane);
+          } else {
+            fill_bias<float>(p, lut_s, rb, h, lane);
+          }
+        }
       }
+      if (lane == 0) {
+        UnitInfo& u = info[slot];
+        u.valid = valid ? 1 : 0;
+        u.b = b;
+        u.h = h;
+        u.q0 = q0;
+        u.t_begin = t_begin;
+        u.nkv = max(t_end - t_begin, 0);
+        u.klen = klen;
+        u.qlen = qlen;
+      }
+      __syncwarp();
+      mbar_arrive(&info_full[slot]);
+      if (!valid) break;
+    }
+  } else if (warp == kLoadWarp) {
+    // ------------------------------------------------------------ TMA producer
+    int gt = 0;          // key tiles issued so far (ring position)
+    int qi = 0;          // units with key tiles so far (Q buffer index)
+    for (int i = 0;; ++i) {
+      const int slot = i & 1;
+      const bool oki = mbar_wait(&info_full[slot], (i >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, oki)) break;
+      const UnitInfo u = info[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&info_empty[slot]);
+      if (!u.valid) break;
+      if (u.nkv == 0) continue;
+      const int qs = qi & 1;
+      if (qi >= 2) {
+        const bool ok = mbar_wait(&q_empty[qs], ((qi - 2) >> 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) break;
+      }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&q_full[qs], kNQ * kTileBytes);
+        for (int g = 0; g < kNQ; ++g)
+          tma_load_4d(smem + kOffQ + (qs * kNQ + g) * kTileBytes, &p.tm_q, &q_full[qs], 0, u.q0 + g * kBM, u.h, u.b);
+      }
+      ++qi;
+      bool stop = false;
+      for (int t = 0; t < u.nkv; ++t, ++gt) {
+        const int s = gt % kStages;
+        const int round = gt / kStages;
+        if (round > 0) {
+          const bool ok = mbar_wait(&kv_empty[s], (round - 1) & 1, abort_flag);
+          if (!__all_sync(0xffffffffu, ok)) { stop = true; break; }
+        }
+        const int k0 = (u.t_begin + t) * kBN;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&k_full[s], kTileBytes);
+          tma_load_4d(smem + kOffK + s * kTileBytes, &p.tm_k, &k_full[s], 0, k0, u.h, u.b);
+          mbar_arrive_expect_tx(&v_full[s], kTileBytes);
+          tma_load_4d(smem + kOffV + s * kTileBytes, &p.tm_v, &v_full[s], 0, k0, u.h, u.b);
+        }
+        if (has_mask) {
+          bool zero = true;
+          const long long base = u.b * p.mk_sb + u.h * p.mk_sh;
+#pragma unroll
+          for (int i2 = 0; i2 < kBN / 32; ++i2) {
+            const int c = lane + 32 * i2;
+            const int n = k0 + c;
+            float mv = 0.f;
+            if (n < p.N) mv = load_any(p.mask, base + n * p.mk_sn, p.mask_dtype);
+            zero = zero && (mv == 0.f);
+            kbias[s * kBN + c] = fmaxf(mv, kMaskFloor) * kLog2e;
+          }
+          zero = __all_sync(0xffffffffu, zero);
+          if (lane == 0) kzero[s] = zero ? 1 : 0;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&k_full[s]);
+        }
+      }
+      if (stop) break;
     }
     // No TMA write may land after this CTA exits: wait for the last fills (already
     // complete on the normal path), ignoring the abort flag but still time-bounded.
     if (lane == 0) {
-      mbar_wait_bounded(q_full, 0);
-      for (int t = max(issued - kStages, 0); t < issued; ++t) {
+      for (int j = max(qi - 2, 0); j < qi; ++j) mbar_wait_bounded(&q_full[j & 1], (j >> 1) & 1);
+      for (int t = max(gt - kStages, 0); t < gt; ++t) {
         mbar_wait_bounded(&k_full[t % kStages], (t / kStages) & 1);
         mbar_wait_bounded(&v_full[t % kStages], (t / kStages) & 1);
       }
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ UMMA issuer
-    if (lane == 0 && nkv > 0) {
+    if (lane == 0) {
       constexpr uint32_t fmt = AbFormat<T>::value;
       constexpr uint32_t idesc_qk = idesc_f16(fmt, kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = idesc_f16(fmt, kBM, kHeadDim, 0, 1);
       const uint32_t sQ = smem_u32(smem + kOffQ);
       const uint32_t sK = smem_u32(smem + kOffK);
       const uint32_t sV = smem_u32(smem + kOffV);
-      auto issue_qk = [&](int g, int s) {
+      auto issue_qk = [&](int g, int qs, int s) {
 #pragma unroll
         for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-          const uint64_t ad = smem_desc_sw128(sQ + g * kTileBytes + kk * 32, 16, 1024);
+          const uint64_t ad = smem_desc_sw128(sQ + (qs * kNQ + g) * kTileBytes + kk * 32, 16, 1024);
           const uint64_t bd = smem_desc_sw128(sK + s * kTileBytes + kk * 32, 16, 1024);
           umma_ss(tmem + 256 * g, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
@@ -326,43 +605,78 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
                   (acc || kk > 0) ? 1u : 0u);
         }
       };
-      // Order per key tile t: as soon as a group has read S(t) into registers, its
-      // S(t+1) = Q K(t+1)^T is issued (it overlaps that group's exponentials); PV(t) is
-      // issued when the group's P(t) is in TMEM.
-      bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
-      if (ok) {
+      // Cursor over this CTA's key tiles in order (units with no tiles are skipped).
+      int ui = 0;          // next unit slot to read
+      int qi = -1;         // Q buffer index of the cursor's unit
+      bool ok = true;
+      auto next_unit = [&](int& nkv) -> bool {   // advances to the next unit with tiles
+        for (;;) {
+          const int slot = ui & 1;
+          if (!mbar_wait(&info_full[slot], (ui >> 1) & 1, abort_flag)) { ok = false; return false; }
+          const int valid = info[slot].valid;
+          nkv = info[slot].nkv;
+          mbar_arrive(&info_empty[slot]);
+          ++ui;
+          if (!valid) return false;
+          if (nkv > 0) { ++qi; return true; }
+        }
+      };
+      int cur_nkv = 0, cur_t = 0;
+      int G = 0;           // global tile index of the cursor
+      // First tile of a unit: S = Q K^T for both groups (the S columns are free).
+      auto start_unit = [&]() -> bool {
+        if (!mbar_wait(&q_full[qi & 1], (qi >> 1) & 1, abort_flag) ||
+            !mbar_wait(&k_full[G % kStages], (G / kStages) & 1, abort_flag))
+          return false;
         tc_fence_after();
-        issue_qk(0, 0);
-        umma_commit(&s_full[0]);
-        issue_qk(1, 0);
-        umma_commit(&s_full[1]);
-        for (int t = 0; t < nkv; ++t) {
-          const int s = t % kStages;
-          const bool has_next = t + 1 < nkv;
-          const int s2 = (t + 1) % kStages;
-          if (has_next && !mbar_wait(&k_full[s2], ((t + 1) / kStages) & 1, abort_flag)) break;
-          if (!mbar_wait(&s_consumed[0], t & 1, abort_flag)) break;
-          if (has_next) {
+        for (int g = 0; g < kNQ; ++g) {
+          issue_qk(g, qi & 1, G % kStages);
+          umma_commit(&s_full[g]);
+        }
+        if (cur_nkv == 1) umma_commit(&q_empty[qi & 1]);
+        return true;
+      };
+      bool have = next_unit(cur_nkv);
+      if (have && ok) ok = start_unit();
+      // Order per key tile G: as soon as a group has read S(G) into registers, its
+      // S(G+1) = Q K(G+1)^T of the same unit is issued (it overlaps that group's
+      // exponentials); PV(G) is issued when the group's P(G) is in TMEM.  The next unit
+      // is looked up only after the last PV of the current one, so a run of units with
+      // no key tiles never waits on a unit slot that this unit still holds; its first QK
+      // is not needed earlier anyway (the softmax threads read O first).  The first PV of
+      // a unit overwrites O: the softmax threads have read the previous unit's O before
+      // they publish that P.
+      while (have && ok) {
+        const int s = G % kStages;
+        const bool more = cur_t + 1 < cur_nkv;
+        const int s2 = (G + 1) % kStages;
+        if (more && !mbar_wait(&k_full[s2], ((G + 1) / kStages) & 1, abort_flag)) break;
+        for (int g = 0; g < kNQ && ok; ++g) {
+          if (!mbar_wait(&s_consumed[g], G & 1, abort_flag)) { ok = false; break; }
+          if (more) {
             tc_fence_after();
-            issue_qk(0, s2);
-            umma_commit(&s_full[0]);
+            issue_qk(g, qi & 1, s2);
+            umma_commit(&s_full[g]);
           }
-          if (!mbar_wait(&s_consumed[1], t & 1, abort_flag)) break;
-          if (has_next) {
-            tc_fence_after();
-            issue_qk(1, s2);
-            umma_commit(&s_full[1]);
-          }
-          if (!mbar_wait(&v_full[s], (t / kStages) & 1, abort_flag)) break;
-          if (!mbar_wait(&p_full[0], t & 1, abort_flag)) break;
+        }
+        if (!ok) break;
+        if (more && cur_t + 2 == cur_nkv) umma_commit(&q_empty[qi & 1]);
+        if (!mbar_wait(&v_full[s], (G / kStages) & 1, abort_flag)) break;
+        for (int g = 0; g < kNQ && ok; ++g) {
+          if (!mbar_wait(&p_full[g], G & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(0, s, t > 0);
-          umma_commit(&pv_done[0]);
-          if (!mbar_wait(&p_full[1], t & 1, abort_flag)) break;
-          tc_fence_after();
-          issue_pv(1, s, t > 0);
-          umma_commit(&pv_done[1]);
-          umma_commit(&kv_empty[s]);
+          issue_pv(g, s, cur_t > 0);
+          umma_commit(&pv_done[g]);
+        }
+        if (!ok) break;
+        umma_commit(&kv_empty[s]);
+        ++G;
+        if (more) {
+          ++cur_t;
+        } else {
+          cur_t = 0;
+          have = next_unit(cur_nkv);
+          if (have && ok) ok = start_unit();
         }
       }
       // Drain: every MMA issued above has completed before TMEM is released.
@@ -374,9 +688,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       }
     }
     __syncwarp();
-    // TMEM is released once both softmax groups are done with it.
+    // TMEM is released once every softmax group is done with it.
     tc_fence_before();
-    named_bar_sync(1, 2 * 128 + 32);
+    named_bar_sync(1, kSoftmaxThreads + 32);
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -388,214 +702,268 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     // ------------------------------------------------------------ softmax groups
     const int g = warp >> 2;                  // query tile
     const int row = (warp & 3) * 32 + lane;   // row inside the tile == TMEM lane
-    const int m = q0 + g * kBM + row;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_off + 256 * g;
     const uint32_t tP = tS + 128;
     const uint32_t tO = tS + 192;
     const float scale_log2 = p.scale_log2;
-
-    const T* pk_row = nullptr;
-    const T* pq_base = nullptr;
-    if (kVariant == kDeberta) {
-      if (p.pos_key != nullptr && m < p.M)
-        pk_row = reinterpret_cast<const T*>(p.pos_key) + b * p.pk_sb + h * p.pk_sh + (long long)m * p.pk_sm;
-      if (p.pos_query != nullptr)
-        pq_base = reinterpret_cast<const T*>(p.pos_query) + b * p.pq_sb + h * p.pq_sh;
-    }
-
-    float m_run = -INFINITY;
-    float l_run = 0.f;
+    int G = 0;                                // global tile index
     bool aborted = false;
-    for (int t = 0; t < nkv; ++t) {
-      const int k0 = (t_begin + t) * kBN;
-      bool ok = mbar_wait(&s_full[g], t & 1, abort_flag);
-      if (has_mask) ok = ok && mbar_wait(&k_full[t % kStages], (t / kStages) & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
-      tc_fence_after();
 
-      // Scores in log2 units.  TMEM is read 32 columns at a time (bounded register
-      // pressure; the asm's memory clobber also keeps each chunk's loads behind its TMEM
-      // load).  x2[j] holds columns 2j, 2j+1.
-      float2 x2[kBN / 2];
-      bool const_bias = false;   // x2 holds raw S; bias `cbias` and scale still to apply
-      float cbias = 0.f;
-      if constexpr (kVariant == kT5) {
-        // Warp-uniform tile class over the warp's 32 rows: r = n - m in [r_lo, r_hi].
-        const int m0 = m - lane;
-        const int r_lo = k0 - (m0 + 31);
-        const int r_hi = k0 + kBN - 1 - m0;
-        const float2 sc2 = make_float2(scale_log2, scale_log2);
-        const bool saturated = (r_lo >= R) || (r_hi <= -R);
-        tmem_ld_x128_f2(tS, x2);
-        tc_fence_before();
-        mbar_arrive(&s_consumed[g]);
-        // The key mask (additive, per key) joins the bias operand of the single FMA pass;
-        // tiles whose mask is all zero skip it.
-        const bool kadd = has_mask && !kzero[t % kStages];
-        const float2* kb2 = reinterpret_cast<const float2*>(kbias + (t % kStages) * kBN);
-        const bool edge = (k0 + kBN > p.N) || (p.causal && r_hi > 0);
-        if (saturated && !kadd && !edge && scale_log2 > 0.f) {
-          // Constant bias: keep raw S; max(s * sc + cb) = max(s) * sc + cb, and the
-          // exponent pass computes s * sc + (cb - m) in one FMA.
-          const_bias = true;
-          cbias = rbias[(r_lo >= R ? 2 * R : 0) + kRPad];
-        } else if (saturated) {
-          const float cb = rbias[(r_lo >= R ? 2 * R : 0) + kRPad];
-          const float2 cb2 = make_float2(cb, cb);
-          if (kadd) {
+    for (int i = 0; !aborted; ++i) {
+      const int slot = i & 1;
+      {
+        const bool oki = mbar_wait(&info_full[slot], (i >> 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, oki)) break;
+      }
+      // Unit fields are re-read from shared memory where they are used, which keeps
+      // them out of the registers held across the tile loop.
+      const volatile UnitInfo* vu = info + slot;
+      if (!vu->valid) break;
+      const int nkv = vu->nkv;
+      const int m = vu->q0 + g * kBM + row;
+
+      float m_run = -INFINITY;
+      float l_run = 0.f;
+      int k0 = vu->t_begin * kBN;
+      for (int t = 0; t < nkv; ++t, ++G, k0 += kBN) {
+        const int st = G % kStages;
+        const float* rbias = rbias_buf + slot * kRBiasLen;
+        bool ok = mbar_wait(&s_full[g], G & 1, abort_flag);
+        if (has_mask) ok = ok && mbar_wait(&k_full[st], (G / kStages) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+        tc_fence_after();
+        // Scores in log2 units.  TMEM is read 32 columns at a time (bounded register
+        // pressure; the asm's memory clobber also keeps each chunk's loads behind its TMEM
+        // load).  x2[j] holds columns 2j, 2j+1.
+        float2 x2[kBN / 2];
+        bool const_bias = false;   // x2 holds raw S; bias `cbias` and scale still to apply
+        float cbias = 0.f;
+        if constexpr (kVariant == kT5) {
+          // Warp-uniform tile class over the warp's 32 rows: r = n - m in [r_lo, r_hi].
+          const int m0 = m - lane;
+          const int r_lo = k0 - (m0 + 31);
+          const int r_hi = k0 + kBN - 1 - m0;
+          const float2 sc2 = make_float2(scale_log2, scale_log2);
+          const bool saturated = (r_lo >= R) || (r_hi <= -R);
+          tmem_ld_2x64_f2(tS, x2);
+          tc_fence_before();
+          mbar_arrive(&s_consumed[g]);
+          // The key mask (additive, per key) joins the bias operand of the single FMA pass;
+          // tiles whose mask is all zero skip it.
+          const bool kadd = has_mask && !kzero[st];
+          const float2* kb2 = reinterpret_cast<const float2*>(kbias + st * kBN);
+          const bool edge = (k0 + kBN > p.N) || (p.causal && r_hi > 0);
+          if (saturated && !kadd && !edge && scale_log2 > 0.f) {
+            // Constant bias: keep raw S; max(s * sc + cb) = max(s) * sc + cb, and the
+            // exponent pass computes s * sc + (cb - m) in one FMA.
+            const_bias = true;
+            cbias = rbias[(r_lo >= R ? 2 * R : 0) + kRPad];
+          } else if (saturated) {
+            const float cb = rbias[(r_lo >= R ? 2 * R : 0) + kRPad];
+            const float2 cb2 = make_float2(cb, cb);
+            if (kadd) {
 #pragma unroll
-            for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(cb2, kb2[j]));
+              for (int j = 0; j < kBN / 2; ++j) {
+                x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(cb2, kb2[j]));
+                if (j % kBiasChunk == kBiasChunk - 1) smem_load_fence();
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, cb2);
+            }
           } else {
+            const float* rb = rbias + (k0 - m + R + kRPad);   // rb[c] = bias of column c
+            if (kadd) {
 #pragma unroll
-            for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, cb2);
+              for (int j = 0; j < kBN / 2; ++j) {
+                x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(make_float2(rb[2 * j], rb[2 * j + 1]), kb2[j]));
+                if (j % kBiasChunk == kBiasChunk - 1) smem_load_fence();
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < kBN / 2; ++j) {
+                x2[j] = __ffma2_rn(x2[j], sc2, make_float2(rb[2 * j], rb[2 * j + 1]));
+                if (j % kBiasChunk == kBiasChunk - 1) smem_load_fence();
+              }
+            }
+          }
+          if (edge) {
+#pragma unroll
+            for (int j = 0; j < kBN / 2; ++j) {
+              const int n = k0 + 2 * j;
+              if (n >= p.N || (p.causal && n > m)) x2[j].x = -INFINITY;
+              if (n + 1 >= p.N || (p.causal && n + 1 > m)) x2[j].y = -INFINITY;
+            }
           }
         } else {
-          const float* rb = rbias + (k0 - m + R + kRPad);   // rb[c] = bias of column c
-          if (kadd) {
+          const int b = vu->b, h = vu->h, klen = vu->klen;
+          const T* pk_row = (p.pos_key != nullptr && m < p.M)
+              ? reinterpret_cast<const T*>(p.pos_key) + b * p.pk_sb + h * p.pk_sh + (long long)m * p.pk_sm
+              : nullptr;
+          const T* pq_base = (p.pos_query != nullptr)
+              ? reinterpret_cast<const T*>(p.pos_query) + b * p.pq_sb + h * p.pq_sh
+              : nullptr;
 #pragma unroll
-            for (int j = 0; j < kBN / 2; ++j)
-              x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(make_float2(rb[2 * j], rb[2 * j + 1]), kb2[j]));
-          } else {
+          for (int ch = 0; ch < kBN / 32; ++ch) {
+            uint32_t sr[32];
+            tmem_ld_x32(tS + 32 * ch, sr);
 #pragma unroll
-            for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, make_float2(rb[2 * j], rb[2 * j + 1]));
-          }
-        }
-        if (edge) {
-#pragma unroll
-          for (int j = 0; j < kBN / 2; ++j) {
-            const int n = k0 + 2 * j;
-            if (n >= p.N || (p.causal && n > m)) x2[j].x = -INFINITY;
-            if (n + 1 >= p.N || (p.causal && n + 1 > m)) x2[j].y = -INFINITY;
-          }
-        }
-      } else {
-#pragma unroll
-        for (int ch = 0; ch < kBN / 32; ++ch) {
-          uint32_t sr[32];
-          tmem_ld_x32(tS + 32 * ch, sr);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = 32 * ch + i;
-            const int n = k0 + c;
-            float xv = -INFINITY;
-            if (n < klen) {
-              float acc = __uint_as_float(sr[i]);
-              const int r = min(max(m - n, -R), R);
-              const int idx = lut_s[r + R];
-              if (pk_row != nullptr) acc += to_f<T>(pk_row[idx * p.pk_sk]);
-              if (pq_base != nullptr) acc += to_f<T>(pq_base[(long long)n * p.pq_sn + idx * p.pq_sk]);
-              xv = acc * scale_log2;
-              if (p.causal && n > m + p.p_seq) xv = -INFINITY;
+            for (int i = 0; i < 32; ++i) {
+              const int c = 32 * ch + i;
+              const int n = k0 + c;
+              float xv = -INFINITY;
+              if (n < klen) {
+                float acc = __uint_as_float(sr[i]);
+                const int r = min(max(m - n, -R), R);
+                const int idx = lut_s[r + R];
+                if (pk_row != nullptr) acc += to_f<T>(pk_row[idx * p.pk_sk]);
+                if (pq_base != nullptr) acc += to_f<T>(pq_base[(long long)n * p.pq_sn + idx * p.pq_sk]);
+                xv = acc * scale_log2;
+                if (p.causal && n > m + p.p_seq) xv = -INFINITY;
+              }
+              if (i & 1) x2[c >> 1].y = xv; else x2[c >> 1].x = xv;
             }
-            if (i & 1) x2[c >> 1].y = xv; else x2[c >> 1].x = xv;
           }
+          tc_fence_before();
+          mbar_arrive(&s_consumed[g]);
         }
-        tc_fence_before();
-        mbar_arrive(&s_consumed[g]);
-      }
-      // Row max: eight independent 3-input max chains.
-      float mx;
-      {
-        float a[8];
+        // Row max: eight independent 3-input max chains.
+        float mx;
+        {
+          float a[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) a[i] = fmaxf(x2[i].x, x2[i].y);
+          for (int i = 0; i < 8; ++i) a[i] = fmaxf(x2[i].x, x2[i].y);
 #pragma unroll
-        for (int j = 8; j < kBN / 2; j += 8) {
+          for (int j = 8; j < kBN / 2; j += 8) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], x2[j + i].x, x2[j + i].y);
+            for (int i = 0; i < 8; ++i) a[i] = fmax3(a[i], x2[j + i].x, x2[j + i].y);
+          }
+          mx = fmaxf(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], fmax3(a[5], a[6], a[7])));
+          if (const_bias) mx = fmaf(mx, scale_log2, cbias);
         }
-        mx = fmaxf(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], fmax3(a[5], a[6], a[7])));
-        if (const_bias) mx = fmaf(mx, scale_log2, cbias);
-      }
 
-      // Online softmax with lazy rescaling: the running max only moves (and O, l are
-      // rescaled) when a row's max grows by more than kRescaleThreshold.
-      const float m_new = fmaxf(m_run, mx);
-      const bool need = m_new > m_run + kRescaleThreshold;
-      if (__any_sync(0xffffffffu, need)) {
-        const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
-        if (t > 0) {
-          // O holds PV(t-1) only once that MMA has completed.
-          const bool okp = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
+        // Online softmax with lazy rescaling: the running max only moves (and O, l are
+        // rescaled) when a row's max grows by more than the threshold.
+        const float m_new = fmaxf(m_run, mx);
+        const bool need = m_new > m_run + RescaleThreshold<T>::value;
+        if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? ex2_approx(m_run - m_new) : 1.f;
+          if (t > 0) {
+            // O holds PV(t-1) only once that MMA has completed.
+            const bool okp = mbar_wait(&pv_done[g], (G - 1) & 1, abort_flag);
+            if (!__all_sync(0xffffffffu, okp)) { aborted = true; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int ch = 0; ch < kHeadDim / 16; ++ch) {
+              uint32_t o[16];
+              tmem_ld_x16(tO + 16 * ch, o);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st_x16(tO + 16 * ch, o);
+            }
+          }
+          l_run *= alpha;
+          if (need) m_run = m_new;
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        // y = x * mul + add: (1, -m) for finished scores, (scale, cbias - m) for raw S.
+        const float2 mul2 = const_bias ? make_float2(scale_log2, scale_log2) : make_float2(1.f, 1.f);
+        const float2 add2 = const_bias ? make_float2(cbias - m_use, cbias - m_use) : make_float2(-m_use, -m_use);
+          float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
+        uint32_t pk[kBN / 2];
+#pragma unroll
+        for (int j = 0; j < kBN / 2; ++j) {
+          const float2 y = __ffma2_rn(x2[j], mul2, add2);
+          // One pair in kPolyEvery goes to the FMA pipe, the rest to the MUFU unit.
+          const float2 e = (j % kPolyEvery == kPolyEvery - 1) ? exp2_poly2(y)
+                                                              : make_float2(ex2_approx(y.x), ex2_approx(y.y));
+          if (j & 1) ls1 = __fadd2_rn(ls1, e); else ls0 = __fadd2_rn(ls0, e);
+          pk[j] = pack2<T>(e.x, e.y);
+        }
+          const float2 ls = __fadd2_rn(ls0, ls1);
+        l_run += ls.x + ls.y;
+        if (G > 0) {
+          // P(G-1) is read by PV(G-1): the P columns are free once it has completed.  The
+          // wait sits after the exponentials, so the PV round trip overlaps them.
+          const bool okp = mbar_wait(&pv_done[g], (G - 1) & 1, abort_flag);
           if (!__all_sync(0xffffffffu, okp)) { aborted = true; break; }
           tc_fence_after();
+        }
+        tmem_st_x64(tP, pk);
+        tc_fence_before();
+        mbar_arrive(&p_full[g]);
+      }
+
+      // Epilogue: O / l, rows past the valid length written as zeros (DeBERTa).  The wait
+      // and the TMEM loads are warp-collective and run on every lane (`aborted` and `nkv`
+      // are warp-uniform).  O has been read out of TMEM before this group's first P of the
+      // next unit is published, so the next unit's first PV (which overwrites O) cannot
+      // start early.
+      bool have = false;
+      if (nkv > 0 && !aborted) {
+        const bool ok = mbar_wait(&pv_done[g], (G - 1) & 1, abort_flag);
+        if (__all_sync(0xffffffffu, ok)) {
+          tc_fence_after();
+          have = true;
+        } else {
+          aborted = true;
+        }
+      }
+      // O rows go to the group's staging tile (128-byte rows, 16-byte chunks XOR-swizzled
+      // by row as the store's SWIZZLE_128B map expects) and leave in one bulk store, so
+      // no generic global store stands in front of this thread's later barrier releases.
+      {
+        const bool row_valid = (kVariant != kDeberta) || (m < vu->qlen);
+        const bool use = have && row_valid && l_run > 0.f;
+        const float inv_l = use ? 1.f / l_run : 0.f;
+        if (row == 0) {
+          bulk_wait_read_all();              // this group's previous store has read the tile
+          mbar_arrive(&stage_free[g]);
+        }
+        const bool okf = mbar_wait(&stage_free[g], i & 1, abort_flag);
+        uint8_t* stg = smem + kOffOStage + g * kTileBytes + row * 128;
+        if (okf) {
+          // O is read 16 columns at a time (`have` is warp-uniform: the load is collective).
 #pragma unroll
           for (int ch = 0; ch < kHeadDim / 16; ++ch) {
             uint32_t o[16];
-            tmem_ld_x16(tO + 16 * ch, o);
+            if (have) {
+              tmem_ld_x16(tO + 16 * ch, o);
+            } else {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st_x16(tO + 16 * ch, o);
+              for (int j = 0; j < 16; ++j) o[j] = 0u;
+            }
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              float f[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[j] = use ? __uint_as_float(o[8 * hf + j]) * inv_l : 0.f;
+              uint4 v;
+              v.x = pack2<T>(f[0], f[1]);
+              v.y = pack2<T>(f[2], f[3]);
+              v.z = pack2<T>(f[4], f[5]);
+              v.w = pack2<T>(f[6], f[7]);
+              *reinterpret_cast<uint4*>(stg + (((2 * ch + hf) ^ (row & 7)) * 16)) = v;
+            }
           }
+          fence_proxy_async_smem();
         }
-        l_run *= alpha;
-        if (need) m_run = m_new;
+        mbar_arrive(&stage_full[g]);
+        if (row == 0 && mbar_wait(&stage_full[g], i & 1, abort_flag)) {
+          tma_store_4d(&p.tm_o, smem + kOffOStage + g * kTileBytes, 0, vu->q0 + g * kBM, vu->h, vu->b);
+          bulk_commit();
+        }
+        if (!__all_sync(0xffffffffu, okf)) aborted = true;
       }
-      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      // y = x * mul + add: (1, -m) for finished scores, (scale, cbias - m) for raw S.
-      const float2 mul2 = const_bias ? make_float2(scale_log2, scale_log2) : make_float2(1.f, 1.f);
-      const float2 add2 = const_bias ? make_float2(cbias - m_use, cbias - m_use) : make_float2(-m_use, -m_use);
-      float2 ls0 = make_float2(0.f, 0.f), ls1 = make_float2(0.f, 0.f);
-      uint32_t pk[kBN / 2];
-#pragma unroll
-      for (int j = 0; j < kBN / 2; ++j) {
-        const float2 y = __ffma2_rn(x2[j], mul2, add2);
-        // One pair in kPolyEvery goes to the FMA pipe, the rest to the MUFU unit.
-        const float2 e = (j % kPolyEvery == kPolyEvery - 1) ? exp2_poly2(y)
-                                                            : make_float2(ex2_approx(y.x), ex2_approx(y.y));
-        if (j & 1) ls1 = __fadd2_rn(ls1, e); else ls0 = __fadd2_rn(ls0, e);
-        pk[j] = pack2<T>(e.x, e.y);
-      }
-      const float2 ls = __fadd2_rn(ls0, ls1);
-      l_run += ls.x + ls.y;
-      if (t > 0) {
-        // P(t-1) is read by PV(t-1): the P columns are free once it has completed.  The
-        // wait sits after the exponentials, so the PV round trip overlaps them.
-        const bool okp = mbar_wait(&pv_done[g], (t - 1) & 1, abort_flag);
-        if (!__all_sync(0xffffffffu, okp)) { aborted = true; break; }
-        tc_fence_after();
-      }
-      tmem_st_x64(tP, pk);
       tc_fence_before();
-      mbar_arrive(&p_full[g]);
-    }
-
-    // Epilogue: O / l, rows past the valid length written as zeros (DeBERTa).  The wait
-    // and the TMEM load are warp-collective and run on every lane (`aborted` and `nkv` are
-    // warp-uniform); only the global store depends on the lane's row.
-    uint32_t o[kHeadDim];
-    bool have = false;
-    if (nkv > 0 && !aborted) {
-      const bool ok = mbar_wait(&pv_done[g], (nkv - 1) & 1, abort_flag);
-      if (__all_sync(0xffffffffu, ok)) {
-        tc_fence_after();
-        tmem_ld_x64(tO, o);
-        have = true;
-      }
-    }
-    if (m < p.M) {
-      T* orow = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * p.o_sh + (long long)m * p.o_sm;
-      const bool row_valid = (kVariant != kDeberta) || (m < qlen);
-      const bool use = have && row_valid && l_run > 0.f;
-      const float inv_l = use ? 1.f / l_run : 0.f;
-#pragma unroll
-      for (int i = 0; i < kHeadDim / 8; ++i) {
-        float f[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] = use ? __uint_as_float(o[8 * i + j]) * inv_l : 0.f;
-        uint4 v;
-        v.x = pack2<T>(f[0], f[1]);
-        v.y = pack2<T>(f[2], f[3]);
-        v.z = pack2<T>(f[4], f[5]);
-        v.w = pack2<T>(f[6], f[7]);
-        *reinterpret_cast<uint4*>(orow + 8 * i) = v;
-      }
+      mbar_arrive(&info_empty[slot]);
     }
   }
 
+  if ((threadIdx.x & (kBM - 1)) == 0) bulk_wait_all();   // this group's O stores have landed
   tc_fence_before();
-  named_bar_sync(1, 2 * 128 + 32);
+  named_bar_sync(1, kSoftmaxThreads + 32);
 }
 
 // Failure-detection self-test: one CTA waits on an mbarrier that nothing ever arrives
@@ -776,12 +1144,18 @@ int launch(vf::KParams* kp, cudaStream_t stream) {
   cudaGetDevice(&dev);
   static std::once_flag flags[64];
   static cudaError_t attr_err[64];
+  static int sm_count[64];
   if (dev < 0 || dev >= 64) return fail(VF_ECUDA, "device ordinal out of range");
   std::call_once(flags[dev], [&] {
     attr_err[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, vf::kSmemAlloc);
+    if (attr_err[dev] == cudaSuccess)
+      attr_err[dev] = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
   });
-  if (attr_err[dev] != cudaSuccess) return fail(VF_ECUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(attr_err[dev]));
-  dim3 grid((kp->M + vf::kNQ * vf::kBM - 1) / (vf::kNQ * vf::kBM), kp->H, kp->B);
+  if (attr_err[dev] != cudaSuccess) return fail(VF_ECUDA, std::string("kernel set-up: ") + cudaGetErrorString(attr_err[dev]));
+  // Persistent launch: one CTA per SM (at most one per unit); each walks its units.
+  const long long units = (long long)((kp->M + vf::kNQ * vf::kBM - 1) / (vf::kNQ * vf::kBM)) * kp->H * kp->B;
+  if (units == 0) return VF_OK;
+  const dim3 grid(static_cast<unsigned>(std::min<long long>(units, std::max(sm_count[dev], 1))));
   kern<<<grid, vf::kThreads, vf::kSmemAlloc, stream>>>(*kp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(VF_ECUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
@@ -864,6 +1238,7 @@ int vf_rpb_attention_fwd(const vf_rpb_attention_args_t* a, void* stream) {
   if ((rc = make_tile_map(&kp.tm_q, a->q, a->dtype, "q"))) return rc;
   if ((rc = make_tile_map(&kp.tm_k, a->k, a->dtype, "k"))) return rc;
   if ((rc = make_tile_map(&kp.tm_v, a->v, a->dtype, "v"))) return rc;
+  if ((rc = make_tile_map(&kp.tm_o, a->out, a->dtype, "out"))) return rc;
   fill_common(&kp, a->q, a->k, a->out);
   kp.scale_log2 = a->softmax_scale * vf::kLog2e;
   kp.causal = a->is_decoder ? 1 : 0;
@@ -923,6 +1298,7 @@ int vf_deberta_attention_fwd(const vf_deberta_attention_args_t* a, void* stream)
   if ((rc = make_tile_map(&kp.tm_q, a->q, a->dtype, "q"))) return rc;
   if ((rc = make_tile_map(&kp.tm_k, a->k, a->dtype, "k"))) return rc;
   if ((rc = make_tile_map(&kp.tm_v, a->v, a->dtype, "v"))) return rc;
+  if ((rc = make_tile_map(&kp.tm_o, a->out, a->dtype, "out"))) return rc;
   fill_common(&kp, a->q, a->k, a->out);
   const float sm_scale = a->has_sm_scale ? a->sm_scale : 1.0f / std::sqrt(static_cast<float>(vf::kHeadDim));
   kp.scale_log2 = sm_scale * vf::kLog2e;

@@ -108,6 +108,21 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Tiled bulk store shared -> global (async proxy), tracked by bulk groups.  Elements
+// outside the tensor's extent are not written.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+               :: "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// The thread's committed bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// The thread's committed bulk stores have completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // ---------------------------------------------------------------- tcgen05: TMEM management
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -243,6 +258,16 @@ __device__ __forceinline__ void tmem_ld_x128_f2(uint32_t taddr, float2 (&x)[64])
                : "r"(taddr) : "memory");
 }
 
+// 128 columns as two x64 loads and one wait: each tcgen05.ld names at most 64
+// destination registers, so the instruction also fits a 128-register launch bound.
+__device__ __forceinline__ void tmem_ld_2x64_f2(uint32_t taddr, float2 (&x)[64]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%128];\n"
+               "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%129];\n"
+               "tcgen05.wait::ld.sync.aligned;\n"
+               : "=f"(x[0].x), "=f"(x[0].y), "=f"(x[1].x), "=f"(x[1].y), "=f"(x[2].x), "=f"(x[2].y), "=f"(x[3].x), "=f"(x[3].y), "=f"(x[4].x), "=f"(x[4].y), "=f"(x[5].x), "=f"(x[5].y), "=f"(x[6].x), "=f"(x[6].y), "=f"(x[7].x), "=f"(x[7].y), "=f"(x[8].x), "=f"(x[8].y), "=f"(x[9].x), "=f"(x[9].y), "=f"(x[10].x), "=f"(x[10].y), "=f"(x[11].x), "=f"(x[11].y), "=f"(x[12].x), "=f"(x[12].y), "=f"(x[13].x), "=f"(x[13].y), "=f"(x[14].x), "=f"(x[14].y), "=f"(x[15].x), "=f"(x[15].y), "=f"(x[16].x), "=f"(x[16].y), "=f"(x[17].x), "=f"(x[17].y), "=f"(x[18].x), "=f"(x[18].y), "=f"(x[19].x), "=f"(x[19].y), "=f"(x[20].x), "=f"(x[20].y), "=f"(x[21].x), "=f"(x[21].y), "=f"(x[22].x), "=f"(x[22].y), "=f"(x[23].x), "=f"(x[23].y), "=f"(x[24].x), "=f"(x[24].y), "=f"(x[25].x), "=f"(x[25].y), "=f"(x[26].x), "=f"(x[26].y), "=f"(x[27].x), "=f"(x[27].y), "=f"(x[28].x), "=f"(x[28].y), "=f"(x[29].x), "=f"(x[29].y), "=f"(x[30].x), "=f"(x[30].y), "=f"(x[31].x), "=f"(x[31].y), "=f"(x[32].x), "=f"(x[32].y), "=f"(x[33].x), "=f"(x[33].y), "=f"(x[34].x), "=f"(x[34].y), "=f"(x[35].x), "=f"(x[35].y), "=f"(x[36].x), "=f"(x[36].y), "=f"(x[37].x), "=f"(x[37].y), "=f"(x[38].x), "=f"(x[38].y), "=f"(x[39].x), "=f"(x[39].y), "=f"(x[40].x), "=f"(x[40].y), "=f"(x[41].x), "=f"(x[41].y), "=f"(x[42].x), "=f"(x[42].y), "=f"(x[43].x), "=f"(x[43].y), "=f"(x[44].x), "=f"(x[44].y), "=f"(x[45].x), "=f"(x[45].y), "=f"(x[46].x), "=f"(x[46].y), "=f"(x[47].x), "=f"(x[47].y), "=f"(x[48].x), "=f"(x[48].y), "=f"(x[49].x), "=f"(x[49].y), "=f"(x[50].x), "=f"(x[50].y), "=f"(x[51].x), "=f"(x[51].y), "=f"(x[52].x), "=f"(x[52].y), "=f"(x[53].x), "=f"(x[53].y), "=f"(x[54].x), "=f"(x[54].y), "=f"(x[55].x), "=f"(x[55].y), "=f"(x[56].x), "=f"(x[56].y), "=f"(x[57].x), "=f"(x[57].y), "=f"(x[58].x), "=f"(x[58].y), "=f"(x[59].x), "=f"(x[59].y), "=f"(x[60].x), "=f"(x[60].y), "=f"(x[61].x), "=f"(x[61].y), "=f"(x[62].x), "=f"(x[62].y), "=f"(x[63].x), "=f"(x[63].y)
+               : "r"(taddr), "r"(taddr + 64u) : "memory");
+}
+
 // tcgen05.st of 16 columns without waiting; the caller issues tmem_wait_st() before the
 // data is consumed.  The source registers are read when the instruction issues.
 __device__ __forceinline__ void tmem_st_x16_nowait(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -310,6 +335,29 @@ __device__ __forceinline__ float2 exp2_poly2(float2 y) {
   q = __ffma2_rn(q, f, make_float2(c0, c0));
   return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
                      __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
+// 2^x for two packed 16-bit values (MUFU, two results per lane and instruction).
+__device__ __forceinline__ uint32_t ex2_bf16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+// acc + lo16(p) and acc + hi16(p) for a packed bf16 pair, accumulated in fp32.
+__device__ __forceinline__ void add_bf16x2_f32(float& acc_lo, float& acc_hi, uint32_t p) {
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "add.rn.f32.bf16 %0, lo, %0;\n\tadd.rn.f32.bf16 %1, hi, %1;\n\t}\n"
+      : "+f"(acc_lo), "+f"(acc_hi) : "r"(p));
+}
+__device__ __forceinline__ void add_f16x2_f32(float& acc_lo, float& acc_hi, uint32_t p) {
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "add.rn.f32.f16 %0, lo, %0;\n\tadd.rn.f32.f16 %1, hi, %1;\n\t}\n"
+      : "+f"(acc_lo), "+f"(acc_hi) : "r"(p));
 }
 
 // Named barrier over `nthreads` threads (a multiple of 32).
