@@ -14,7 +14,7 @@
 //   warp  8    TMA producer (Q per unit, double-buffered; a 3-stage K/V ring across units)
 //   warp  9    UMMA issuer (one elected lane) + TMEM allocation
 //   warp  10   unit preparation (schedule, live key span, per-head bias table), one unit ahead
-//   warp  11   idle
+//   warp  11   UMMA issuer for group 1 (warp 9 then serves group 0)
 // Register split after the prologue: see kRegsSoftmax / kRegsProducer.
 // TMEM (512 columns, fp32): per query tile g, S at 256g, P (bf16 pairs) at 256g+128,
 // O at 256g+192.  S = Q K^T and O += P V run on tcgen05.mma (kind::f16, fp32 accumulate);
@@ -62,6 +62,13 @@ static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsProducer == 384 * 168, "setmax
 constexpr int kLoadWarp = kSoftmaxWarps;
 constexpr int kMmaWarp = kSoftmaxWarps + 1;
 constexpr int kPrepWarp = kSoftmaxWarps + 2;
+constexpr int kMmaWarp2 = kSoftmaxWarps + 3;
+#ifndef VF_MMA_ISSUERS
+#define VF_MMA_ISSUERS 2
+#endif
+// UMMA issuing warps: 2 = one per softmax group (warps 9 and 11), so neither group's
+// MMAs wait behind the other's in one instruction stream; 1 = warp 9 issues for both.
+constexpr int kMmaIssuers = VF_MMA_ISSUERS;
 constexpr uint32_t kTmemCols = 256 * kNQ;
 constexpr int kMaxRel = 1024;               // relative-position table radius limit
 constexpr int kMaxLut = 2 * kMaxRel + 1;
@@ -363,9 +370,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&q_full[s], 1);
-      mbar_init(&q_empty[s], 1);
+      mbar_init(&q_empty[s], kMmaIssuers);
       mbar_init(&info_full[s], 32);
-      mbar_init(&info_empty[s], kSoftmaxThreads + 2);
+      mbar_init(&info_empty[s], kSoftmaxThreads + 1 + kMmaIssuers);
       mbar_init(&stage_free[s], 1);
       mbar_init(&stage_full[s], kBM);
     }
@@ -378,9 +385,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&k_full[s], has_mask ? 2 : 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], kMmaIssuers);
     }
-    mbar_init(drain, 1);
+    mbar_init(drain, kMmaIssuers);
     misc->abort_flag = 0;
     fence_mbar_init();
   }
@@ -580,8 +587,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         mbar_wait_bounded(&v_full[t % kStages], (t / kStages) & 1);
       }
     }
-  } else if (warp == kMmaWarp) {
+  } else if (warp == kMmaWarp || (kMmaIssuers == 2 && warp == kMmaWarp2)) {
     // ------------------------------------------------------------ UMMA issuer
+    // Serves softmax groups [g_lo, g_hi).
+    const int g_lo = (kMmaIssuers == 2 && warp == kMmaWarp2) ? 1 : 0;
+    const int g_hi = kMmaIssuers == 2 ? g_lo + 1 : kNQ;
     if (lane == 0) {
       constexpr uint32_t fmt = AbFormat<T>::value;
       constexpr uint32_t idesc_qk = idesc_f16(fmt, kBM, kBN, 0, 0);
@@ -629,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             !mbar_wait(&k_full[G % kStages], (G / kStages) & 1, abort_flag))
           return false;
         tc_fence_after();
-        for (int g = 0; g < kNQ; ++g) {
+        for (int g = g_lo; g < g_hi; ++g) {
           issue_qk(g, qi & 1, G % kStages);
           umma_commit(&s_full[g]);
         }
@@ -651,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         const bool more = cur_t + 1 < cur_nkv;
         const int s2 = (G + 1) % kStages;
         if (more && !mbar_wait(&k_full[s2], ((G + 1) / kStages) & 1, abort_flag)) break;
-        for (int g = 0; g < kNQ && ok; ++g) {
+        for (int g = g_lo; g < g_hi && ok; ++g) {
           if (!mbar_wait(&s_consumed[g], G & 1, abort_flag)) { ok = false; break; }
           if (more) {
             tc_fence_after();
@@ -662,7 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         if (!ok) break;
         if (more && cur_t + 2 == cur_nkv) umma_commit(&q_empty[qi & 1]);
         if (!mbar_wait(&v_full[s], (G / kStages) & 1, abort_flag)) break;
-        for (int g = 0; g < kNQ && ok; ++g) {
+        for (int g = g_lo; g < g_hi && ok; ++g) {
           if (!mbar_wait(&p_full[g], G & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
           issue_pv(g, s, cur_t > 0);
@@ -688,11 +698,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       }
     }
     __syncwarp();
-    // TMEM is released once every softmax group is done with it.
+    // TMEM is released once every softmax group and issuer is done with it.
     tc_fence_before();
-    named_bar_sync(1, kSoftmaxThreads + 32);
+    named_bar_sync(1, kSoftmaxThreads + 32 * kMmaIssuers);
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
   }
   return;
   }
@@ -963,7 +973,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 
   if ((threadIdx.x & (kBM - 1)) == 0) bulk_wait_all();   // this group's O stores have landed
   tc_fence_before();
-  named_bar_sync(1, kSoftmaxThreads + 32);
+  named_bar_sync(1, kSoftmaxThreads + 32 * kMmaIssuers);
 }
 
 // Failure-detection self-test: one CTA waits on an mbarrier that nothing ever arrives
