@@ -79,13 +79,6 @@ constexpr float kMaskFloor = -1.0e30f;      // masks are clamped here before sca
 #define VF_RESCALE_BF16 32.0f
 #endif
 constexpr int kPolyEvery = 3;               // every 3rd exponential pair on the FMA pipe
-#ifndef VF_BIAS_CHUNK
-#define VF_BIAS_CHUNK 16
-#endif
-// Bias-table loads are issued kBiasChunk column pairs at a time: the compiler may not
-// hoist more of them ahead of their use (each holds registers next to the 128 scores).
-constexpr int kBiasChunk = VF_BIAS_CHUNK;
-__device__ __forceinline__ void smem_load_fence() { asm volatile("" ::: "memory"); }
 
 enum Variant : int { kT5 = 0, kDeberta = 1 };
 
@@ -126,7 +119,8 @@ constexpr int kRPad = 160;                  // bias-table padding: a warp's wind
 constexpr int kRBiasLen = (kMaxLut + 2 * kRPad + 3) & ~3;
 constexpr int kOffKBias = kOffOStage + kNQ * kTileBytes;
 constexpr int kOffKZero = kOffKBias + kStages * kBN * 4;         // per stage: key mask all zero
-constexpr int kOffRBias = kOffKZero + 16;
+constexpr int kOffZeroRow = kOffKZero + 16;                      // kBN zero floats
+constexpr int kOffRBias = kOffZeroRow + kBN * 4;
 constexpr int kOffLut = kOffRBias + 2 * kRBiasLen * 4;
 constexpr int kOffBar = (kOffLut + kMaxLut * 2 + 15) & ~15;
 // barriers: q_full[2], q_empty[2], s_full[2], p_full[2], s_consumed[2], pv_done[2],
@@ -341,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   float* kbias = reinterpret_cast<float*>(smem + kOffKBias);
   float* rbias_buf = reinterpret_cast<float*>(smem + kOffRBias);   // [2][kRBiasLen], index r + R + kRPad
   int* kzero = reinterpret_cast<int*>(smem + kOffKZero);
+  float* zero_row = reinterpret_cast<float*>(smem + kOffZeroRow);
   short* lut_s = reinterpret_cast<short*>(smem + kOffLut);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* q_full = bars + 0;        // [2] Q tiles of a unit are in shared memory
@@ -403,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   }
   // Relative-position lookup table (the same for every unit).
   for (int i = tid; i <= 2 * R; i += kThreads) lut_s[i] = p.lut[i];
+  if (tid < kBN) zero_row[tid] = 0.f;
   // T5 mask samples for the unit costs (one load per thread for typical sizes).
   if (has_mask && lpt_enabled<kVariant>(p)) {
     uint8_t* live = smem + kOffLive;
@@ -769,34 +765,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             // exponent pass computes s * sc + (cb - m) in one FMA.
             const_bias = true;
             cbias = rbias[(r_lo >= R ? 2 * R : 0) + kRPad];
-          } else if (saturated) {
-            const float cb = rbias[(r_lo >= R ? 2 * R : 0) + kRPad];
-            const float2 cb2 = make_float2(cb, cb);
-            if (kadd) {
-#pragma unroll
-              for (int j = 0; j < kBN / 2; ++j) {
-                x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(cb2, kb2[j]));
-                if (j % kBiasChunk == kBiasChunk - 1) smem_load_fence();
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, cb2);
-            }
           } else {
-            const float* rb = rbias + (k0 - m + R + kRPad);   // rb[c] = bias of column c
-            if (kadd) {
+            // One FMA pass: x = s * scale + (bias[c] + key mask[c]).  rb[c] is the bias of
+            // column c; a saturated window reads a constant run of the table's padding.
+            // Tiles whose key mask is all zero read a zero row instead of the mask.
+            const float* rb = saturated ? rbias + (r_lo >= R ? 2 * R + kRPad : 0)
+                                        : rbias + (k0 - m + R + kRPad);
+            const float2* kb = kadd ? kb2 : reinterpret_cast<const float2*>(zero_row);
 #pragma unroll
-              for (int j = 0; j < kBN / 2; ++j) {
-                x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(make_float2(rb[2 * j], rb[2 * j + 1]), kb2[j]));
-                if (j % kBiasChunk == kBiasChunk - 1) smem_load_fence();
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < kBN / 2; ++j) {
-                x2[j] = __ffma2_rn(x2[j], sc2, make_float2(rb[2 * j], rb[2 * j + 1]));
-                if (j % kBiasChunk == kBiasChunk - 1) smem_load_fence();
-              }
-            }
+            for (int j = 0; j < kBN / 2; ++j)
+              x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(make_float2(rb[2 * j], rb[2 * j + 1]), kb[j]));
           }
           if (edge) {
 #pragma unroll
