@@ -30,6 +30,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -117,6 +118,7 @@ constexpr int kOffV = kOffK + kStages * kTileBytes;
 constexpr int kOffOStage = kOffV + kStages * kTileBytes;
 constexpr int kRPad = 160;                  // bias-table padding: a warp's window never clamps
 constexpr int kRBiasLen = (kMaxLut + 2 * kRPad + 3) & ~3;
+
 constexpr int kOffKBias = kOffOStage + kNQ * kTileBytes;
 constexpr int kOffKZero = kOffKBias + kStages * kBN * 4;         // per stage: key mask all zero
 constexpr int kOffZeroRow = kOffKZero + 16;                      // kBN zero floats
@@ -142,6 +144,10 @@ struct SmemMisc {
   int abort_flag;
 };
 static_assert(kSmemAlloc <= 227 * 1024, "shared memory over the per-CTA limit");
+
+// One zero position value: the gather of a missing DeBERTa position term reads it with
+// stride 0 (read-only; never written).
+__device__ const uint16_t g_zero_pos = 0;
 
 template <typename T> __device__ __forceinline__ float to_f(T v);
 template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
@@ -786,35 +792,48 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           }
         } else {
           const int b = vu->b, h = vu->h, klen = vu->klen;
-          const T* pk_row = (p.pos_key != nullptr && m < p.M)
-              ? reinterpret_cast<const T*>(p.pos_key) + b * p.pk_sb + h * p.pk_sh + (long long)m * p.pk_sm
-              : nullptr;
-          const T* pq_base = (p.pos_query != nullptr)
-              ? reinterpret_cast<const T*>(p.pos_query) + b * p.pq_sb + h * p.pq_sh
-              : nullptr;
-#pragma unroll
-          for (int ch = 0; ch < kBN / 32; ++ch) {
-            uint32_t sr[32];
-            tmem_ld_x32(tS + 32 * ch, sr);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int c = 32 * ch + i;
-              const int n = k0 + c;
-              float xv = -INFINITY;
-              if (n < klen) {
-                float acc = __uint_as_float(sr[i]);
-                const int r = min(max(m - n, -R), R);
-                const int idx = lut_s[r + R];
-                if (pk_row != nullptr) acc += to_f<T>(pk_row[idx * p.pk_sk]);
-                if (pq_base != nullptr) acc += to_f<T>(pq_base[(long long)n * p.pq_sn + idx * p.pq_sk]);
-                xv = acc * scale_log2;
-                if (p.causal && n > m + p.p_seq) xv = -INFINITY;
-              }
-              if (i & 1) x2[c >> 1].y = xv; else x2[c >> 1].x = xv;
-            }
-          }
+          // Position terms.  A missing term (or a row past M) reads one zero element with
+          // stride 0, so the gather loop has no branches and its loads can be in flight
+          // together (a per-column branch around each gather serialised them: ~1.9x
+          // slower).
+          const T* zero = reinterpret_cast<const T*>(&g_zero_pos);
+          const bool pk_on = p.pos_key != nullptr && m < p.M;
+          const T* pk_row = pk_on ? reinterpret_cast<const T*>(p.pos_key) + b * p.pk_sb + h * p.pk_sh + (long long)m * p.pk_sm
+                                  : zero;
+          const long long pk_sk = pk_on ? p.pk_sk : 0;
+          const bool pq_on = p.pos_query != nullptr;
+          const T* pq_bh = pq_on ? reinterpret_cast<const T*>(p.pos_query) + b * p.pq_sb + h * p.pq_sh : zero;
+          const long long pq_sn = pq_on ? p.pq_sn : 0, pq_sk = pq_on ? p.pq_sk : 0;
+          // S first (one TMEM read, so QK of the next tile can start), then the terms.
+          tmem_ld_2x64_f2(tS, x2);
           tc_fence_before();
           mbar_arrive(&s_consumed[g]);
+          // Warp-uniform: where the index is r + const over the warp's whole window
+          // (DeBERTa's exact bucket range), it is computed instead of looked up.
+          const int m0 = m - lane;
+          const int r_lo = m0 - (k0 + kBN - 1), r_hi = m0 + 31 - k0;
+          bool linear = r_lo >= -R && r_hi <= R;
+          int off = 0;
+          if (linear) {
+            off = lut_s[r_lo + R] - r_lo;
+            linear = (lut_s[r_hi + R] - r_hi) == off;
+          }
+#pragma unroll
+          for (int c = 0; c < kBN; ++c) {
+            const int n = min(k0 + c, klen - 1);   // keys past klen are masked below
+            const int idx = linear ? m - n + off : lut_s[min(max(m - n, -R), R) + R];
+            const float add = to_f<T>(pk_row[idx * pk_sk]) + to_f<T>(pq_bh[(long long)n * pq_sn + idx * pq_sk]);
+            if (c & 1) x2[c >> 1].y = (x2[c >> 1].y + add) * scale_log2;
+            else x2[c >> 1].x = (x2[c >> 1].x + add) * scale_log2;
+          }
+          if (k0 + kBN > klen || p.causal) {
+#pragma unroll
+            for (int j = 0; j < kBN / 2; ++j) {
+              const int n = k0 + 2 * j;
+              if (n >= klen || (p.causal && n > m + p.p_seq)) x2[j].x = -INFINITY;
+              if (n + 1 >= klen || (p.causal && n + 1 > m + p.p_seq)) x2[j].y = -INFINITY;
+            }
+          }
         }
         // Row max: eight independent 3-input max chains.
         float mx;
@@ -1300,6 +1319,7 @@ int vf_deberta_attention_fwd(const vf_deberta_attention_args_t* a, void* stream)
       return fail(VF_EINVAL, "deberta attention: pos_key must be (B, H, M, 2*ATT_SPAN)");
     kp.pos_key = t.data;
     kp.pk_sb = t.stride[0]; kp.pk_sh = t.stride[1]; kp.pk_sm = t.stride[2]; kp.pk_sk = t.stride[3];
+
   }
   if (a->pos_query.data != nullptr) {
     const vf_tensor4d_t& t = a->pos_query;
@@ -1307,6 +1327,7 @@ int vf_deberta_attention_fwd(const vf_deberta_attention_args_t* a, void* stream)
       return fail(VF_EINVAL, "deberta attention: pos_query must be (B, H, N, 2*ATT_SPAN)");
     kp.pos_query = t.data;
     kp.pq_sb = t.stride[0]; kp.pq_sh = t.stride[1]; kp.pq_sn = t.stride[2]; kp.pq_sk = t.stride[3];
+
   }
   // Log buckets exactly when the reference's torch path uses them
   // (kernels/flash_deberta_attention.py:400).
