@@ -122,8 +122,7 @@ constexpr int kRBiasLen = (kMaxLut + 2 * kRPad + 3) & ~3;
 constexpr int kOffKBias = kOffOStage + kNQ * kTileBytes;
 constexpr int kOffKZero = kOffKBias + kStages * kBN * 4;         // per stage: key mask all zero
 constexpr int kOffZeroRow = kOffKZero + 16;                      // kBN zero floats
-constexpr int kOffRBias = kOffZeroRow + kBN * 4;
-constexpr int kOffLut = kOffRBias + 2 * kRBiasLen * 4;
+constexpr int kOffLut = kOffZeroRow + kBN * 4;
 constexpr int kOffBar = (kOffLut + kMaxLut * 2 + 15) & ~15;
 // barriers: q_full[2], q_empty[2], s_full[2], p_full[2], s_consumed[2], pv_done[2],
 // info_full[2], info_empty[2], stage_free[2], stage_full[2], k_full/v_full/kv_empty[kStages],
@@ -135,9 +134,14 @@ constexpr int kMaxLptPairs = 1024;          // (batch, query block) pairs ordere
 constexpr int kMaxLptSamples = 2048;        // T5 mask samples (batch x key tile) for the costs
 constexpr int kOffOrder = kOffInfo + 2 * 64;                      // uint16_t[kMaxLptPairs]
 constexpr int kOffCost = kOffOrder + 2 * kMaxLptPairs;            // uint8_t[kMaxLptPairs]
+// T5-only tables last: the DeBERTa kernel requests shared memory up to kOffLive only, which
+// leaves the SM more L1 cache for its position-term gathers.
 constexpr int kOffLive = kOffCost + kMaxLptPairs;                 // uint8_t[kMaxLptSamples]
-constexpr int kSmemBytes = kOffLive + kMaxLptSamples;
+constexpr int kOffRBias = (kOffLive + kMaxLptSamples + 15) & ~15;  // float[2][kRBiasLen]
+constexpr int kSmemBytes = kOffRBias + 2 * kRBiasLen * 4;
 constexpr int kSmemAlloc = kSmemBytes + 1024;
+constexpr int kSmemAllocDeberta = kOffLive + 1024;
+template <int kVariant> constexpr int smem_alloc() { return kVariant == kT5 ? kSmemAlloc : kSmemAllocDeberta; }
 
 struct SmemMisc {
   uint32_t tmem_base;
@@ -1154,7 +1158,7 @@ int launch(vf::KParams* kp, cudaStream_t stream) {
   static int sm_count[64];
   if (dev < 0 || dev >= 64) return fail(VF_ECUDA, "device ordinal out of range");
   std::call_once(flags[dev], [&] {
-    attr_err[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, vf::kSmemAlloc);
+    attr_err[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, vf::smem_alloc<kVariant>());
     if (attr_err[dev] == cudaSuccess)
       attr_err[dev] = cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
   });
@@ -1163,7 +1167,7 @@ int launch(vf::KParams* kp, cudaStream_t stream) {
   const long long units = (long long)((kp->M + vf::kNQ * vf::kBM - 1) / (vf::kNQ * vf::kBM)) * kp->H * kp->B;
   if (units == 0) return VF_OK;
   const dim3 grid(static_cast<unsigned>(std::min<long long>(units, std::max(sm_count[dev], 1))));
-  kern<<<grid, vf::kThreads, vf::kSmemAlloc, stream>>>(*kp);
+  kern<<<grid, vf::kThreads, vf::smem_alloc<kVariant>(), stream>>>(*kp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(VF_ECUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
   return VF_OK;
