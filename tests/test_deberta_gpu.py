@@ -143,3 +143,18 @@ def test_deberta_c1_config_subset():
                                            w["pos_key"][b:b + 1].float().cpu(), w["pos_query"][b:b + 1].float().cpu(),
                                            False, w["sm_scale"], 256, 512, True)
         assert_close(out[b:b + 1], ref, lens_mask(sl, out.shape[2]), what=f"C1 batch {b}")
+
+
+def test_deberta_fp32_inputs_tf32_level():
+    """fp32 inputs (BASELINE C1's dtype): fp16 operands, fp32 softmax/accumulation, fp32 out."""
+    q, k, v, pk, pq, sl = make(2, 2, 320, 320, 256, dtype=torch.float32, lens=[320, 200], seed=23)
+    dev = torch.device("cuda")
+    cu = lambda t: None if t is None else t.to(dev)
+    out = _op()(cu(q), cu(k), cu(v), cu(sl), cu(pk), cu(pq), False, 1.0 / math.sqrt(64 * 3), 256, 512, True)
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float32 and out.shape == q.shape
+    ref = oracle.deberta_attention_ref(q, k, v, sl, pk, pq, False, 1.0 / math.sqrt(64 * 3), 256, 512, True)
+    valid = lens_mask(sl, 320)
+    err, cos = assert_close(out, ref, valid, max_abs=2e-3, min_cos=0.99999, what="fp32 inputs")
+    print(f"fp32 deberta: max_abs {err:.3e} min_cos {cos:.7f}")
+    assert (out.float().cpu()[(~valid)[:, None, :].expand(out.shape[:3])] == 0).all()

@@ -3,7 +3,14 @@
 // Tensors are read here (sizes, strides, data pointers, the current CUDA stream) and
 // passed as plain pointers/sizes to vf_rpb_attention_fwd / vf_deberta_attention_fwd; the
 // kernels, bucket tables and validation live behind the C ABI.  Only the output tensor is
-// allocated.  CPU tensors raise: there is no CPU implementation.
+// allocated (plus fp16 copies for fp32 inputs, below).  CPU tensors raise: there is no CPU
+// implementation.
+//
+// fp32 q / k / v (and DeBERTa position tensors) are computed in fp16: the tensor cores take
+// 16-bit operands, and fp16 keeps the 10-bit mantissa of TF32, the precision the reference's
+// fp32 Triton path multiplies at.  Inputs are clamped to the fp16 range (+-65504) on the way
+// in; scores, softmax and accumulation stay fp32 inside the kernel; the output is returned
+// in fp32.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -61,6 +68,12 @@ void check_rc(int rc) {
   TORCH_CHECK(rc == VF_OK, "vf_b200 error ", rc, ": ", vf_last_error());
 }
 
+// fp32 operands become fp16 (clamped to its finite range); 16-bit ones pass through.
+at::Tensor to_kernel_dtype(const at::Tensor& t) {
+  if (t.scalar_type() != at::kFloat) return t;
+  return at::clamp(t, -65504.0, 65504.0).to(at::kHalf);
+}
+
 at::Tensor rpb_attention(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
                          const std::optional<at::Tensor>& rpb_table, int64_t num_buckets,
                          int64_t max_distance, bool is_decoder,
@@ -72,7 +85,9 @@ at::Tensor rpb_attention(const at::Tensor& q_in, const at::Tensor& k_in, const a
   TORCH_CHECK(q_in.scalar_type() == k_in.scalar_type() && q_in.scalar_type() == v_in.scalar_type(),
               "vf_b200: q, k, v must share a dtype");
   c10::cuda::CUDAGuard guard(q_in.device());
-  const at::Tensor q = tma_ready(q_in), k = tma_ready(k_in), v = tma_ready(v_in);
+  const bool f32 = q_in.scalar_type() == at::kFloat;
+  const at::Tensor q = tma_ready(to_kernel_dtype(q_in)), k = tma_ready(to_kernel_dtype(k_in)),
+                   v = tma_ready(to_kernel_dtype(v_in));
   at::Tensor out = make_out(q);
   vf_rpb_attention_args_t a{};
   a.dtype = dtype_code(q);
@@ -102,7 +117,7 @@ at::Tensor rpb_attention(const at::Tensor& q_in, const at::Tensor& k_in, const a
   a.dropout_p = static_cast<float>(dropout_p);
   a.softmax_scale = static_cast<float>(softmax_scale);
   check_rc(vf_rpb_attention_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
-  return out;
+  return f32 ? out.to(at::kFloat) : out;
 }
 
 at::Tensor deberta_attention(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
@@ -117,7 +132,9 @@ at::Tensor deberta_attention(const at::Tensor& q_in, const at::Tensor& k_in, con
   TORCH_CHECK(q_in.scalar_type() == k_in.scalar_type() && q_in.scalar_type() == v_in.scalar_type(),
               "vf_b200: q, k, v must share a dtype");
   c10::cuda::CUDAGuard guard(q_in.device());
-  const at::Tensor q = tma_ready(q_in), k = tma_ready(k_in), v = tma_ready(v_in);
+  const bool f32 = q_in.scalar_type() == at::kFloat;
+  const at::Tensor q = tma_ready(to_kernel_dtype(q_in)), k = tma_ready(to_kernel_dtype(k_in)),
+                   v = tma_ready(to_kernel_dtype(v_in));
   at::Tensor out = make_out(q);
   vf_deberta_attention_args_t a{};
   a.dtype = dtype_code(q);
@@ -133,15 +150,18 @@ at::Tensor deberta_attention(const at::Tensor& q_in, const at::Tensor& k_in, con
     TORCH_CHECK(lens.numel() == q.size(0), "vf_b200: seq_lengths must have one entry per batch row");
     a.seq_lengths = lens.data_ptr<int32_t>();
   }
+  at::Tensor pk, pq;   // keep fp16 copies alive until the launch is enqueued
   if (pos_key.has_value()) {
     require_cuda(*pos_key, "pos_key");
-    TORCH_CHECK(pos_key->scalar_type() == q.scalar_type(), "vf_b200: pos_key must have the dtype of q");
-    a.pos_key = view4(*pos_key);
+    TORCH_CHECK(pos_key->scalar_type() == q_in.scalar_type(), "vf_b200: pos_key must have the dtype of q");
+    pk = to_kernel_dtype(*pos_key);
+    a.pos_key = view4(pk);
   }
   if (pos_query.has_value()) {
     require_cuda(*pos_query, "pos_query");
-    TORCH_CHECK(pos_query->scalar_type() == q.scalar_type(), "vf_b200: pos_query must have the dtype of q");
-    a.pos_query = view4(*pos_query);
+    TORCH_CHECK(pos_query->scalar_type() == q_in.scalar_type(), "vf_b200: pos_query must have the dtype of q");
+    pq = to_kernel_dtype(*pos_query);
+    a.pos_query = view4(pq);
   }
   a.causal = causal ? 1 : 0;
   a.has_sm_scale = sm_scale.has_value() ? 1 : 0;
@@ -150,7 +170,7 @@ at::Tensor deberta_attention(const at::Tensor& q_in, const at::Tensor& k_in, con
   a.max_relative_distance = static_cast<int32_t>(max_relative_distance);
   a.use_log_bucket = use_log_bucket ? 1 : 0;
   check_rc(vf_deberta_attention_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
-  return out;
+  return f32 ? out.to(at::kFloat) : out;
 }
 
 // Shape functions for tracing (torch.compile / fake tensors).
