@@ -136,6 +136,13 @@ def build_workload(name: str, rank: int, device):
             base = W.deberta_attention_inputs(seed=2000 + rank, device=device)
             cfg = {"workload": "C1 DeBERTa-v3-large disentangled layer (bf16 on GPU), c2p|p2c, 256 buckets",
                    "global_batch": 8, "seq_len": 512, "lengths": "U[64,512] right-padded"}
+        elif name == "deberta_c1_fp32":
+            # BASELINE C1's own dtype: fp32 tensors in and out; the op computes with fp16
+            # operands (TF32's mantissa) and fp32 softmax / accumulation.
+            base = W.deberta_attention_inputs(seed=2000 + rank, device=device, dtype=torch.float32)
+            cfg = {"workload": "C1 DeBERTa-v3-large disentangled layer, fp32 inputs and output, c2p|p2c, 256 buckets",
+                   "global_batch": 8, "seq_len": 512, "lengths": "U[64,512] right-padded",
+                   "_dtype": "f32 in/out (fp16 operands, fp32 accumulate)"}
         else:
             L = int(name.split("_")[-1])
             base = W.deberta_attention_inputs(seed=3000 + rank, device=device, B=16384 // L, L=L,
@@ -325,6 +332,7 @@ def main():
         return
 
     peaks = measured_peaks()
+    dtype_label = cfg.pop("_dtype", "bf16")
     achieved = flops / (ms / args.steps * 1e-3) / 1e12      # this rank's launches
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16"], "traffic": committed_traffic(args.workload),
@@ -332,7 +340,7 @@ def main():
                 "algorithmic_flops_per_launch": flops}
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
+            "vs_baseline": None, "dtype": dtype_label, "data": "synthetic", "config": cfg,
             "tokens_per_s": tokens_all * args.steps / (ms_max * 1e-3),
             "pct_bf16_peak": value / (peaks["bf16"] * world),
             "roofline": roofline, "gpu_launches": args.steps, "clocks": clocks, "e2e": e2e}

@@ -158,3 +158,11 @@ def test_deberta_fp32_inputs_tf32_level():
     err, cos = assert_close(out, ref, valid, max_abs=2e-3, min_cos=0.99999, what="fp32 inputs")
     print(f"fp32 deberta: max_abs {err:.3e} min_cos {cos:.7f}")
     assert (out.float().cpu()[(~valid)[:, None, :].expand(out.shape[:3])] == 0).all()
+
+
+def test_deberta_many_short_sequences_natural_order():
+    """More (batch, query block) pairs than the cost-ordering table holds, some of length 0."""
+    B, L = 1100, 64
+    lens = [(29 * b) % (L + 1) for b in range(B)]
+    q, k, v, pk, pq, sl = make(B, 1, L, L, 32, lens=lens, seed=33)
+    run(q, k, v, pk, pq, sl, sm_scale=0.125, pb=32, mr=64, log=True, what="1100 sequences")

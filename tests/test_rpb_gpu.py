@@ -167,3 +167,12 @@ def test_rpb_fp32_inputs_tf32_level():
         ref = oracle.rpb_attention_ref(q, k, v, t, 32, 128, False, m, scale)
         err, cos = assert_close(out, ref, None, max_abs=max_abs, min_cos=min_cos, what=f"fp32 inputs, scale {scale}")
         print(f"fp32 rpb scale {scale}: max_abs {err:.3e} min_cos {cos:.7f}")
+
+
+def test_rpb_many_short_sequences_natural_order():
+    """More (batch, query block) pairs than the cost-ordering table holds: the kernel deals
+    the units in natural order instead; results must not change."""
+    B, L = 1100, 64
+    lens = [1 + (37 * b) % L for b in range(B)]
+    q, k, v, t, m = make_inputs(B, 1, L, L, torch.bfloat16, lens=lens, seed=31)
+    check(q, k, v, t, m, what="1100 sequences")
