@@ -130,6 +130,22 @@ def build_workload(name: str, rank: int, device):
                "global_batch": 16, "seq_len": 768, "heads": 16, "head_dim": 64,
                "lengths": "U[256,768] right-padded"}
         keys = ("q", "k", "v", "rpb_table", "padding_mask")
+    elif name == "mt5_c2_varlen":
+        # C2's sequences packed back to back (cu_seqlens), no padding rows or mask.
+        from kernels.flash_attention_rpb import flash_attention_rpb_varlen
+        base = W.mt5_varlen_inputs(seed=1000 + rank, device=device)
+        lens = base["lengths"].tolist()
+        flops = W.core_flops(lens)
+
+        def call(x):
+            return flash_attention_rpb_varlen(x["q"], x["k"], x["v"], x["cu_seqlens"], x["max_seqlen"],
+                                              x["rpb_table"], 32, 128, False, 1.0)
+
+        per_set = sum(base[k].numel() * base[k].element_size() for k in ("q", "k", "v")) * 4 // 3
+        cfg = {"workload": "C2 mT5-large encoder self-attention layer, T5 RPB 32 buckets/128, packed (cu_seqlens)",
+               "global_batch": 16, "seq_len": 768, "heads": 16, "head_dim": 64,
+               "lengths": "U[256,768] packed, no padding"}
+        keys = ("q", "k", "v", "rpb_table", "cu_seqlens")
     elif name.startswith("deberta_c1") or name.startswith("deberta_c5"):
         from kernels.flash_deberta_attention import flash_deberta_attention
         if name == "deberta_c1":
@@ -176,7 +192,7 @@ def cpu_baseline(name: str, lens, budget_s: float = 12.0):
     from vf_b200 import workloads as W
     torch.set_num_threads(os.cpu_count() or 1)
     cores = torch.get_num_threads()
-    if name == "mt5_c2":
+    if name.startswith("mt5_c2"):
         x = W.mt5_attention_inputs(seed=1000, device="cpu")
         flops_done, t0, n = 0.0, time.perf_counter(), 0
         while True:

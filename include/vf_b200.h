@@ -76,6 +76,21 @@ typedef struct {
 
 int vf_rpb_attention_fwd(const vf_rpb_attention_args_t* args, void* stream);
 
+/* Packed variable-length batch of the same operator: sequence s occupies rows
+ * [cu_seqlens[s], cu_seqlens[s+1]) of q, k, v and out, and attends only within itself.
+ * Replaces the flat-as-one-sequence call of plugins/mt5_gliner/model.py:178-192 (which
+ * lets the requests of one batch attend to each other) and the pad/unpad round trip
+ * around kernels/flash_attention_rpb.py:296; the reference has no packed entry point.
+ *
+ * q, k, v, out: views of size (1, H, total, 64) (a [total, H, 64] tensor has strides
+ * (total*H*64, 64, H*64, 1)); k has the rows of q.  cu_seqlens: device int32[num_seqs+1],
+ * non-decreasing, cu_seqlens[0] >= 0, cu_seqlens[num_seqs] <= total.  max_seqlen: host
+ * bound >= every sequence length (sizes the bucket table and the work list).  padding_mask
+ * must be absent.  Rows of out outside every sequence are not written.  Offsets that break
+ * these rules set bit 2 of vf_device_error(); the rows used are clamped into the views. */
+int vf_rpb_attention_varlen_fwd(const vf_rpb_attention_args_t* args, const int32_t* cu_seqlens,
+                                int32_t num_seqs, int32_t max_seqlen, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * DeBERTa disentangled attention (c2p + p2c relative-position scores).
  * Replaces kernels/flash_deberta_attention.py:455 `flash_deberta_attention(q, k, v,
@@ -126,7 +141,8 @@ int vf_deberta_log_bucket(int32_t bucket_size, int32_t max_position,
 const char* vf_last_error(void);
 
 /* Reads (and optionally clears) the device error word of the current device: bit 0 = a
- * bounded in-kernel wait ran out of time, bit 1 = a gather index failed its bounds check.
+ * bounded in-kernel wait ran out of time, bit 1 = a gather index failed its bounds check,
+ * bit 2 = packed-batch offsets broke the rules of vf_rpb_attention_varlen_fwd.
  * Synchronises the device.  Returns the word (>= 0) or VF_ECUDA. */
 int vf_device_error(int32_t clear);
 

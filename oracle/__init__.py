@@ -9,7 +9,8 @@ It restates, in plain PyTorch on the CPU, the reference's own algorithms for the
   * T5 bucket:        models/mt5/mt5_encoder.py:125-148 (T5RelativePositionBias._relative_position_bucket)
   * T5 dense bias:    models/mt5/mt5_encoder.py:150-164 + :75-110 (_make_contiguous_additive_bias)
   * T5 attention:     models/mt5/mt5_encoder.py:309-316 (SDPA, scale=1.0), equal in exact
-                      arithmetic to kernels/flash_attention_rpb.py:62-230
+                      arithmetic to kernels/flash_attention_rpb.py:62-230; the packed form
+                      applies it to each cu_seqlens sequence alone
   * DeBERTa bucket:   models/deberta_v2/deberta_v2_encoder.py:70-89 (make_log_bucket_position)
   * DeBERTa op:       kernels/flash_deberta_attention.py:375-448 (_pytorch_flash_deberta_fwd),
                       with the Triton kernel's row semantics (rows >= seq_len are 0,
@@ -25,6 +26,7 @@ from .rpb import (  # noqa: F401
     deberta_layer_ref,
     deberta_log_bucket_ref,
     rpb_attention_ref,
+    rpb_attention_varlen_ref,
     t5_bias_dense_ref,
     t5_relative_bucket_ref,
 )

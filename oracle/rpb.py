@@ -108,6 +108,27 @@ def rpb_attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return torch.matmul(p, v.to(dtype))
 
 
+def rpb_attention_varlen_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens,
+                             rpb_table: Optional[torch.Tensor], num_buckets: int, max_distance: int,
+                             is_decoder: bool, softmax_scale: float = 1.0, dtype=torch.float64,
+                             fill: float = float("nan")) -> torch.Tensor:
+    """Packed batch: q, k, v [total, H, 64]; sequence s = rows cu_seqlens[s]:cu_seqlens[s+1]
+    attends only within itself, i.e. rpb_attention_ref on that sequence alone with no
+    padding mask (the per-request call models/mt5/mt5_encoder.py:309-316 makes for one
+    unpadded request).  Rows outside every sequence are `fill`."""
+    cu = [int(x) for x in torch.as_tensor(cu_seqlens).tolist()]
+    out = torch.full(q.shape, fill, dtype=dtype)
+    for s in range(len(cu) - 1):
+        a, b = cu[s], cu[s + 1]
+        if b <= a:
+            continue
+        seq = lambda t: t[a:b].permute(1, 0, 2).unsqueeze(0)     # (1, H, L, 64)
+        o = rpb_attention_ref(seq(q), seq(k), seq(v), rpb_table, num_buckets, max_distance, is_decoder,
+                              None, softmax_scale, dtype=dtype)
+        out[a:b] = o[0].permute(1, 0, 2)
+    return out
+
+
 # ---------------------------------------------------------------------------- DeBERTa
 def deberta_attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                           seq_lengths: Optional[torch.Tensor] = None,

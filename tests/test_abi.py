@@ -111,3 +111,33 @@ def test_deberta_validation_rejects_before_launch():
     a.max_relative_distance = 0
     assert lib.vf_deberta_attention_fwd(ctypes.byref(a), None) == _lib.VF_EINVAL
     assert "position" in lib.vf_last_error().decode()
+
+
+def _varlen_args(total=300, H=4):
+    a = _rpb_args()
+    a.q, a.k, a.v, a.out = (_fake_t4((1, H, total, 64), 0x10000 * (i + 1)) for i in range(4))
+    return a
+
+
+@pytest.mark.parametrize("mutate,cu,num_seqs,max_seqlen,code,msg", [
+    (None, None, 2, 100, _lib.VF_EINVAL, "cu_seqlens"),
+    (None, 0x20003, 2, 100, _lib.VF_EINVAL, "cu_seqlens"),          # misaligned
+    (None, 0x20000, 0, 100, _lib.VF_EINVAL, "num_seqs"),
+    (None, 0x20000, 2, 0, _lib.VF_EINVAL, "max_seqlen"),
+    (None, 0x20000, 2, 301, _lib.VF_EINVAL, "max_seqlen"),
+    ("batch2", 0x20000, 2, 100, _lib.VF_EINVAL, "packed views"),
+    ("k_rows", 0x20000, 2, 100, _lib.VF_EINVAL, "packed rows"),
+    ("mask", 0x20000, 2, 100, _lib.VF_EUNSUPPORTED, "padding_mask"),
+])
+def test_rpb_varlen_validation_rejects_before_launch(mutate, cu, num_seqs, max_seqlen, code, msg):
+    lib = _lib.load()
+    a = _varlen_args()
+    if mutate == "batch2":
+        a.q.size[0] = 2
+    elif mutate == "k_rows":
+        a.k.size[2] = 299
+    elif mutate == "mask":
+        a.padding_mask = _fake_t4((1, 1, 1, 300), 0x80000)
+    rc = lib.vf_rpb_attention_varlen_fwd(ctypes.byref(a), cu, num_seqs, max_seqlen, None)
+    assert rc == code
+    assert msg in lib.vf_last_error().decode()

@@ -5,6 +5,9 @@
 //                s = scale * q.k + rpb_table[bucket(n - m), h] + padding_mask[b, h, n]
 //   * kDeberta — kernels/flash_deberta_attention.py:145-299 (_flash_deberta_fwd_kernel):
 //                s = sm_scale * (q.k + pos_key[m, idx(m - n)] + pos_query[n, idx(m - n)])
+//     kT5 also runs over a packed batch (KParams::cu_seqlens set): sequence b is rows
+//     [cu_seqlens[b], cu_seqlens[b+1]) of q/k/v/out and attends only within itself (no
+//     counterpart in the reference, which pads; no mask)
 //
 // Persistent launch: one CTA per SM walks a list of work units; a unit is 256 query rows
 // of one (batch, head) as two 128-row tiles, against that batch's live 128-key tiles.
@@ -104,6 +107,11 @@ struct __align__(64) KParams {
   const void* pos_query;
   long long pq_sb, pq_sh, pq_sn, pq_sk;
   const int* seq_lengths;
+  // Packed variable-length batch (T5): sequence b is rows [cu_seqlens[b], cu_seqlens[b+1])
+  // of the single packed "batch" of the q/k/v/out views; B = number of sequences and
+  // M = N = the longest sequence.  nullptr: padded (B, H, L, D) layout.
+  const int* cu_seqlens;
+  int packed_rows;       // rows of the packed views (bound of every cu_seqlens entry)
   int p_seq;             // N - M (causal offset)
   int span2;             // 2 * ATT_SPAN, bound of the position index
   short lut[kMaxLut];    // T5: bucket of r = n - m;  DeBERTa: idx of r = m - n
@@ -279,9 +287,39 @@ struct UnitInfo {
   int valid;             // 0: the CTA's work list has ended
   int b, h, q0;
   int t_begin, nkv;      // key tiles [t_begin, t_begin + nkv)
-  int klen, qlen;        // valid keys / rows (DeBERTa seq_len; T5: N and M)
+  int klen, qlen;        // valid keys / rows (DeBERTa seq_len; T5: N and M, or the sequence)
 };
-static_assert(sizeof(UnitInfo) <= 64, "unit slot");
+// The packed layout's first row of the unit's sequence sits beside the slots, in its own
+// int[2] (a larger UnitInfo costs the softmax warps registers).
+constexpr int kOffInfoRow0 = 96;
+static_assert(2 * sizeof(UnitInfo) <= kOffInfoRow0, "unit slots");
+
+// Rows of sequence b: valid keys / query rows and the first row in the tensor views.
+// Padded layout: every row of batch b (DeBERTa: up to seq_len), from row 0.  Packed layout:
+// the cu_seqlens range of the views' single batch.
+struct SeqGeo {
+  int klen, qlen, row0;
+};
+template <int kVariant>
+__device__ __forceinline__ SeqGeo seq_geo(const KParams& p, int b) {
+  SeqGeo s{p.N, p.M, 0};
+  if (kVariant == kDeberta && p.seq_lengths != nullptr) {
+    const int L = __ldg(p.seq_lengths + b);
+    s.klen = min(max(L, 0), p.N);
+    s.qlen = min(max(L, 0), p.M);
+  }
+  if (kVariant == kT5 && p.cu_seqlens != nullptr) {
+    // Offsets outside [0, packed_rows], decreasing offsets or a sequence longer than
+    // max_seqlen set the error word; the rows used are clamped into the views either way.
+    const int r0 = __ldg(p.cu_seqlens + b), r1 = __ldg(p.cu_seqlens + b + 1);
+    if (r0 < 0 || r1 < r0 || r1 > p.packed_rows || r1 - r0 > p.M) atomicOr(&g_vf_error, kErrBadInput);
+    const int lo = min(max(r0, 0), p.packed_rows);
+    const int L = min(min(max(r1, lo), p.packed_rows) - lo, p.M);
+    s.klen = s.qlen = L;
+    s.row0 = lo;
+  }
+  return s;
+}
 
 // Whether the CTA orders its units by cost: the (batch, query block) pairs and, for a
 // T5 mask, the (batch, key tile) mask samples must fit the shared-memory tables.
@@ -300,16 +338,12 @@ __device__ __forceinline__ bool lpt_enabled(const KParams& p) {
 template <int kVariant>
 __device__ int pair_cost(const KParams& p, const uint8_t* live, int b, int qb) {
   const int q0 = qb * (kNQ * kBM);
-  int klen = p.N, qlen = p.M;
-  if (kVariant == kDeberta && p.seq_lengths != nullptr) {
-    const int L = __ldg(p.seq_lengths + b);
-    klen = min(max(L, 0), p.N);
-    qlen = min(max(L, 0), p.M);
-  }
-  if (kVariant == kDeberta && q0 >= qlen) return 0;
+  const SeqGeo sg = seq_geo<kVariant>(p, b);
+  const int klen = sg.klen, qlen = sg.qlen;
+  if ((kVariant == kDeberta || p.cu_seqlens != nullptr) && q0 >= qlen) return 0;
   int t_end = (klen + kBN - 1) / kBN;
   if (p.causal) {
-    const int last_key = min(q0 + kNQ * kBM, p.M) - 1 + p.p_seq;
+    const int last_key = min(q0 + kNQ * kBM, qlen) - 1 + p.p_seq;
     t_end = min(t_end, last_key < 0 ? 0 : last_key / kBN + 1);
   }
   int n = t_end;
@@ -364,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint64_t* drain = kv_empty + kStages;
   SmemMisc* misc = reinterpret_cast<SmemMisc*>(smem + kOffMisc);
   UnitInfo* info = reinterpret_cast<UnitInfo*>(smem + kOffInfo);   // [2]
+  int* info_row0 = reinterpret_cast<int*>(smem + kOffInfo + kOffInfoRow0);   // [2]
   volatile int* abort_flag = &misc->abort_flag;
 
   const int tid = threadIdx.x;
@@ -465,13 +500,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       }
       int b = 0, h = 0, q0 = 0;
       const bool valid = unit_coords(p, lpt ? order : nullptr, i, b, h, q0);
-      int klen = p.N, qlen = p.M, t_begin = 0, t_end = 0;
+      int klen = p.N, qlen = p.M, t_begin = 0, t_end = 0, row0 = 0;
       if (valid) {
-        if (kVariant == kDeberta && p.seq_lengths != nullptr) {
-          const int L = __ldg(p.seq_lengths + b);
-          klen = min(max(L, 0), p.N);
-          qlen = min(max(L, 0), p.M);
-        }
+        const SeqGeo sg = seq_geo<kVariant>(p, b);
+        klen = sg.klen;
+        qlen = sg.qlen;
+        row0 = sg.row0;
         t_end = (klen + kBN - 1) / kBN;
         if (has_mask) {
           // The span of keys whose mask is alive bounds the key tiles worth visiting.
@@ -493,10 +527,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         }
         if (p.causal) {
           // Keys a row may see: n <= m + p_seq, m < q0 + kNQ * kBM.
-          const int last_key = min(q0 + kNQ * kBM, p.M) - 1 + p.p_seq;
+          const int last_key = min(q0 + kNQ * kBM, qlen) - 1 + p.p_seq;
           t_end = min(t_end, last_key < 0 ? 0 : last_key / kBN + 1);
         }
         if (kVariant == kDeberta && q0 >= qlen) t_end = t_begin;   // rows all padded: zeros only
+        if (p.cu_seqlens != nullptr && q0 >= qlen) t_end = t_begin;   // packed: no rows here at all
         if (kVariant == kT5) {
           float* rb = rbias_buf + slot * kRBiasLen;
           if (p.table == nullptr) {
@@ -520,6 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         u.nkv = max(t_end - t_begin, 0);
         u.klen = klen;
         u.qlen = qlen;
+        info_row0[slot] = row0;
       }
       __syncwarp();
       mbar_arrive(&info_full[slot]);
@@ -534,6 +570,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       const bool oki = mbar_wait(&info_full[slot], (i >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, oki)) break;
       const UnitInfo u = info[slot];
+      const int row0 = info_row0[slot];
+      const int bc = p.cu_seqlens != nullptr ? 0 : u.b;   // batch coordinate in the views
       __syncwarp();
       if (lane == 0) mbar_arrive(&info_empty[slot]);
       if (!u.valid) break;
@@ -546,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       if (lane == 0) {
         mbar_arrive_expect_tx(&q_full[qs], kNQ * kTileBytes);
         for (int g = 0; g < kNQ; ++g)
-          tma_load_4d(smem + kOffQ + (qs * kNQ + g) * kTileBytes, &p.tm_q, &q_full[qs], 0, u.q0 + g * kBM, u.h, u.b);
+          tma_load_4d(smem + kOffQ + (qs * kNQ + g) * kTileBytes, &p.tm_q, &q_full[qs], 0, row0 + u.q0 + g * kBM, u.h, bc);
       }
       ++qi;
       bool stop = false;
@@ -560,9 +598,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         const int k0 = (u.t_begin + t) * kBN;
         if (lane == 0) {
           mbar_arrive_expect_tx(&k_full[s], kTileBytes);
-          tma_load_4d(smem + kOffK + s * kTileBytes, &p.tm_k, &k_full[s], 0, k0, u.h, u.b);
+          tma_load_4d(smem + kOffK + s * kTileBytes, &p.tm_k, &k_full[s], 0, row0 + k0, u.h, bc);
           mbar_arrive_expect_tx(&v_full[s], kTileBytes);
-          tma_load_4d(smem + kOffV + s * kTileBytes, &p.tm_v, &v_full[s], 0, k0, u.h, u.b);
+          tma_load_4d(smem + kOffV + s * kTileBytes, &p.tm_v, &v_full[s], 0, row0 + k0, u.h, bc);
         }
         if (has_mask) {
           bool zero = true;
@@ -769,7 +807,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           // tiles whose mask is all zero skip it.
           const bool kadd = has_mask && !kzero[st];
           const float2* kb2 = reinterpret_cast<const float2*>(kbias + st * kBN);
-          const bool edge = (k0 + kBN > p.N) || (p.causal && r_hi > 0);
+          const int klen = vu->klen;
+          const bool edge = (k0 + kBN > klen) || (p.causal && r_hi > 0);
           if (saturated && !kadd && !edge && scale_log2 > 0.f) {
             // Constant bias: keep raw S; max(s * sc + cb) = max(s) * sc + cb, and the
             // exponent pass computes s * sc + (cb - m) in one FMA.
@@ -790,8 +829,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
 #pragma unroll
             for (int j = 0; j < kBN / 2; ++j) {
               const int n = k0 + 2 * j;
-              if (n >= p.N || (p.causal && n > m)) x2[j].x = -INFINITY;
-              if (n + 1 >= p.N || (p.causal && n + 1 > m)) x2[j].y = -INFINITY;
+              if (n >= klen || (p.causal && n > m)) x2[j].x = -INFINITY;
+              if (n + 1 >= klen || (p.causal && n + 1 > m)) x2[j].y = -INFINITY;
             }
           }
         } else {
@@ -921,6 +960,45 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           aborted = true;
         }
       }
+      if (p.cu_seqlens != nullptr) {
+        // Packed batch: the next sequence's rows follow this one's, so a 128-row tile store
+        // could overwrite them.  Each thread stages its own row (unswizzled) and copies it
+        // with one 128-byte bulk copy if the row belongs to the sequence.
+        const bool mine = m < vu->qlen;     // units past the sequence's end write nothing
+        const bool use = have && mine && l_run > 0.f;
+        const float inv_l = use ? 1.f / l_run : 0.f;
+        bulk_wait_read_all();                // this thread's previous row copy has read its row
+        uint8_t* srow = smem + kOffOStage + g * kTileBytes + row * 128;
+#pragma unroll
+        for (int ch = 0; ch < kHeadDim / 16; ++ch) {
+          uint32_t o[16];
+          if (have) {
+            tmem_ld_x16(tO + 16 * ch, o);    // collective: every lane, whatever its row
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] = 0u;
+          }
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            float f[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) f[j] = use ? __uint_as_float(o[8 * hf + j]) * inv_l : 0.f;
+            uint4 v;
+            v.x = pack2<T>(f[0], f[1]);
+            v.y = pack2<T>(f[2], f[3]);
+            v.z = pack2<T>(f[4], f[5]);
+            v.w = pack2<T>(f[6], f[7]);
+            if (mine) *reinterpret_cast<uint4*>(srow + (2 * ch + hf) * 16) = v;
+          }
+        }
+        if (mine) {
+          fence_proxy_async_smem();
+          T* dst = reinterpret_cast<T*>(p.out) + vu->h * p.o_sh +
+                   (long long)(reinterpret_cast<const volatile int*>(smem + kOffInfo + kOffInfoRow0)[slot] + m) * p.o_sm;
+          bulk_copy_s2g(dst, srow, kHeadDim * 2);
+          bulk_commit();
+        }
+      } else
       // O rows go to the group's staging tile (128-byte rows, 16-byte chunks XOR-swizzled
       // by row as the store's SWIZZLE_128B map expects) and leave in one bulk store, so
       // no generic global store stands in front of this thread's later barrier releases.
@@ -972,7 +1050,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     }
   }
 
-  if ((threadIdx.x & (kBM - 1)) == 0) bulk_wait_all();   // this group's O stores have landed
+  // This thread's O stores have landed (tile stores: one thread per group; packed rows:
+  // every thread).
+  if (p.cu_seqlens != nullptr || (threadIdx.x & (kBM - 1)) == 0) bulk_wait_all();
   tc_fence_before();
   named_bar_sync(1, kSoftmaxThreads + 32 * kMmaIssuers);
 }
@@ -1184,6 +1264,52 @@ void fill_common(vf::KParams* kp, const vf_tensor4d_t& q, const vf_tensor4d_t& k
   kp->N = static_cast<int>(k.size[2]);
 }
 
+// Shared set-up of the two T5 entry points: operand checks, tensor maps, scale, table
+// pointer.  Leaves the mask, the bucket table and (packed layout) the geometry to the caller.
+int rpb_prepare(const vf_rpb_attention_args_t* a, vf::KParams* kp) {
+  if (a->dtype != VF_DTYPE_BF16 && a->dtype != VF_DTYPE_F16)
+    return fail(VF_EUNSUPPORTED, "rpb attention: q/k/v dtype must be float16 or bfloat16");
+  int rc = check_qkv(a->q, a->k, a->v, a->out);
+  if (rc) return rc;
+  if (a->dropout_p != 0.0f) return fail(VF_EUNSUPPORTED, "rpb attention: dropout_p must be 0 (inference path)");
+  const int H = static_cast<int>(a->q.size[1]);
+  std::memset(kp, 0, offsetof(vf::KParams, lut));
+  if ((rc = make_tile_map(&kp->tm_q, a->q, a->dtype, "q"))) return rc;
+  if ((rc = make_tile_map(&kp->tm_k, a->k, a->dtype, "k"))) return rc;
+  if ((rc = make_tile_map(&kp->tm_v, a->v, a->dtype, "v"))) return rc;
+  if ((rc = make_tile_map(&kp->tm_o, a->out, a->dtype, "out"))) return rc;
+  fill_common(kp, a->q, a->k, a->out);
+  kp->scale_log2 = a->softmax_scale * vf::kLog2e;
+  kp->causal = a->is_decoder ? 1 : 0;
+  kp->p_seq = 0;
+  if (a->rpb_table != nullptr) {
+    if (a->table_cols != H) return fail(VF_EINVAL, "rpb_table must be [num_buckets, heads]");
+    if (a->table_rows <= 0) return fail(VF_EINVAL, "rpb_table has no rows");
+    kp->table = a->rpb_table;
+    kp->tb_srow = a->table_stride_row;
+    kp->tb_scol = a->table_stride_col;
+    kp->table_dtype = a->table_dtype;
+  }
+  const int half = a->is_decoder ? a->num_buckets : a->num_buckets / 2;
+  if (half / 2 < 1 || a->max_distance <= half / 2)
+    return fail(VF_EUNSUPPORTED, "rpb attention: bucket configuration outside the T5 formula's domain");
+  return VF_OK;
+}
+
+// Bucket lookup table for relative positions |n - m| < span, clamped to the table's rows.
+int finish_rpb_table(const vf_rpb_attention_args_t* a, int span, vf::KParams* kp) {
+  const int nb = static_cast<int>(a->rpb_table ? a->table_rows : a->num_buckets);
+  const RelTable& tab = t5_table(a->num_buckets, a->max_distance, !a->is_decoder, span);
+  if (tab.R > vf::kMaxRel) return fail(VF_EUNSUPPORTED, "rpb attention: relative-position table too large");
+  kp->rel_R = tab.R;
+  for (int i = 0; i <= 2 * tab.R; ++i) {
+    int v = tab.lut[i];
+    v = std::min(std::max(v, 0), nb - 1);   // kernels/flash_attention_rpb.py:162 clamp to the table
+    kp->lut[i] = static_cast<short>(v);
+  }
+  return VF_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1237,45 +1363,10 @@ int vf_deberta_log_bucket(int32_t bucket_size, int32_t max_position, int32_t rmi
 
 int vf_rpb_attention_fwd(const vf_rpb_attention_args_t* a, void* stream) {
   if (a == nullptr) return fail(VF_EINVAL, "null args");
-  if (a->dtype != VF_DTYPE_BF16 && a->dtype != VF_DTYPE_F16)
-    return fail(VF_EUNSUPPORTED, "rpb attention: q/k/v dtype must be float16 or bfloat16");
-  int rc = check_qkv(a->q, a->k, a->v, a->out);
-  if (rc) return rc;
-  if (a->dropout_p != 0.0f) return fail(VF_EUNSUPPORTED, "rpb attention: dropout_p must be 0 (inference path)");
-  const int H = static_cast<int>(a->q.size[1]);
-  const int M = static_cast<int>(a->q.size[2]), N = static_cast<int>(a->k.size[2]);
   static thread_local vf::KParams kp;
-  std::memset(&kp, 0, offsetof(vf::KParams, lut));
-  if ((rc = make_tile_map(&kp.tm_q, a->q, a->dtype, "q"))) return rc;
-  if ((rc = make_tile_map(&kp.tm_k, a->k, a->dtype, "k"))) return rc;
-  if ((rc = make_tile_map(&kp.tm_v, a->v, a->dtype, "v"))) return rc;
-  if ((rc = make_tile_map(&kp.tm_o, a->out, a->dtype, "out"))) return rc;
-  fill_common(&kp, a->q, a->k, a->out);
-  kp.scale_log2 = a->softmax_scale * vf::kLog2e;
-  kp.causal = a->is_decoder ? 1 : 0;
-  kp.p_seq = 0;
-  if (a->rpb_table != nullptr) {
-    if (a->table_cols != H) return fail(VF_EINVAL, "rpb_table must be [num_buckets, heads]");
-    if (a->table_rows <= 0) return fail(VF_EINVAL, "rpb_table has no rows");
-    kp.table = a->rpb_table;
-    kp.tb_srow = a->table_stride_row;
-    kp.tb_scol = a->table_stride_col;
-    kp.table_dtype = a->table_dtype;
-  }
-  const int nb = static_cast<int>(a->rpb_table ? a->table_rows : a->num_buckets);
-  {
-    const int half = a->is_decoder ? a->num_buckets : a->num_buckets / 2;
-    if (half / 2 < 1 || a->max_distance <= half / 2)
-      return fail(VF_EUNSUPPORTED, "rpb attention: bucket configuration outside the T5 formula's domain");
-  }
-  const RelTable& tab = t5_table(a->num_buckets, a->max_distance, !a->is_decoder, std::max(M, N));
-  if (tab.R > vf::kMaxRel) return fail(VF_EUNSUPPORTED, "rpb attention: relative-position table too large");
-  kp.rel_R = tab.R;
-  for (int i = 0; i <= 2 * tab.R; ++i) {
-    int v = tab.lut[i];
-    v = std::min(std::max(v, 0), nb - 1);   // kernels/flash_attention_rpb.py:162 clamp to the table
-    kp.lut[i] = static_cast<short>(v);
-  }
+  int rc = rpb_prepare(a, &kp);
+  if (rc) return rc;
+  const int H = kp.H, N = kp.N;
   if (a->padding_mask.data != nullptr) {
     const vf_tensor4d_t& mk = a->padding_mask;
     if (mk.size[2] != 1 && mk.stride[2] != 0)
@@ -1289,6 +1380,31 @@ int vf_rpb_attention_fwd(const vf_rpb_attention_args_t* a, void* stream) {
     kp.mk_sn = mk.size[3] > 1 ? mk.stride[3] : 0;
     kp.mask_dtype = a->mask_dtype;
   }
+  if ((rc = finish_rpb_table(a, std::max(kp.M, kp.N), &kp))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return a->dtype == VF_DTYPE_BF16 ? launch<vf::kT5, __nv_bfloat16>(&kp, s) : launch<vf::kT5, __half>(&kp, s);
+}
+
+int vf_rpb_attention_varlen_fwd(const vf_rpb_attention_args_t* a, const int32_t* cu_seqlens, int32_t num_seqs,
+                                int32_t max_seqlen, void* stream) {
+  if (a == nullptr) return fail(VF_EINVAL, "null args");
+  if (cu_seqlens == nullptr || (reinterpret_cast<uintptr_t>(cu_seqlens) & 3) != 0)
+    return fail(VF_EINVAL, "rpb varlen: cu_seqlens must be a non-null, 4-byte aligned device int32 array");
+  if (num_seqs <= 0 || num_seqs > 65535) return fail(VF_EINVAL, "rpb varlen: num_seqs must be in [1, 65535]");
+  if (a->q.size[0] != 1) return fail(VF_EINVAL, "rpb varlen: q/k/v/out must be packed views of size (1, H, total, 64)");
+  if (a->k.size[2] != a->q.size[2]) return fail(VF_EINVAL, "rpb varlen: k and q must have the same packed rows");
+  if (a->padding_mask.data != nullptr)
+    return fail(VF_EUNSUPPORTED, "rpb varlen: the packed layout takes no padding_mask (sequences are exact)");
+  if (max_seqlen <= 0 || max_seqlen > a->q.size[2])
+    return fail(VF_EINVAL, "rpb varlen: max_seqlen must be in [1, total rows]");
+  static thread_local vf::KParams kp;
+  int rc = rpb_prepare(a, &kp);
+  if (rc) return rc;
+  kp.cu_seqlens = cu_seqlens;
+  kp.packed_rows = kp.M;
+  kp.B = num_seqs;
+  kp.M = kp.N = max_seqlen;
+  if ((rc = finish_rpb_table(a, max_seqlen, &kp))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return a->dtype == VF_DTYPE_BF16 ? launch<vf::kT5, __nv_bfloat16>(&kp, s) : launch<vf::kT5, __half>(&kp, s);
 }

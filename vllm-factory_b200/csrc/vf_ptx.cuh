@@ -14,6 +14,7 @@ __device__ unsigned int g_vf_error;
 enum : unsigned int {
   kErrWaitTimeout = 1u << 0,   // an mbarrier wait exceeded its cycle budget
   kErrBadIndex    = 1u << 1,   // a gather index failed its bounds check (skipped)
+  kErrBadInput    = 1u << 2,   // an input broke a documented limit (e.g. a sequence longer than max_seqlen)
 };
 
 // A wait that has spun this many SM cycles (~1 s at 1.9 GHz) gives up and flags an error.
@@ -114,6 +115,12 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
   asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
                :: "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
                : "memory");
+}
+// Untiled bulk copy shared -> global (async proxy), bulk-group completion; addresses
+// 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_copy_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+               :: "l"(reinterpret_cast<uint64_t>(dst)), "r"(smem_u32(src)), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // The thread's committed bulk stores have finished reading shared memory.

@@ -16,6 +16,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <algorithm>
+#include <climits>
 #include <cmath>
 #include <optional>
 #include <string>
@@ -120,6 +122,74 @@ at::Tensor rpb_attention(const at::Tensor& q_in, const at::Tensor& k_in, const a
   return f32 ? out.to(at::kFloat) : out;
 }
 
+// Packed batch: q, k, v are [total, H, 64] (the rows of every sequence back to back),
+// cu_seqlens int32 [num_seqs + 1]; the kernel sees them as (1, H, total, 64) views.
+at::Tensor rpb_attention_varlen(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
+                                const at::Tensor& cu_seqlens, int64_t max_seqlen,
+                                const std::optional<at::Tensor>& rpb_table, int64_t num_buckets,
+                                int64_t max_distance, bool is_decoder, double softmax_scale) {
+  require_cuda(q_in, "q");
+  require_cuda(k_in, "k");
+  require_cuda(v_in, "v");
+  require_cuda(cu_seqlens, "cu_seqlens");
+  TORCH_CHECK(q_in.dim() == 3 && k_in.dim() == 3 && v_in.dim() == 3, "vf_b200: packed q, k, v must be [total, heads, 64]");
+  TORCH_CHECK(q_in.scalar_type() == k_in.scalar_type() && q_in.scalar_type() == v_in.scalar_type(),
+              "vf_b200: q, k, v must share a dtype");
+  TORCH_CHECK(cu_seqlens.dim() == 1 && cu_seqlens.numel() >= 2, "vf_b200: cu_seqlens must be [num_seqs + 1]");
+  c10::cuda::CUDAGuard guard(q_in.device());
+  const bool f32 = q_in.scalar_type() == at::kFloat;
+  // (total, H, D) -> (1, H, total, D) views; TMA wants unit innermost stride and 16-byte rows.
+  auto packed = [](const at::Tensor& t) {
+    at::Tensor x = to_kernel_dtype(t);
+    if (x.stride(2) != 1 || (x.stride(0) * x.element_size()) % 16 != 0 || (x.stride(1) * x.element_size()) % 16 != 0 ||
+        (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) != 0)
+      x = x.contiguous();
+    return x;
+  };
+  const at::Tensor q = packed(q_in), k = packed(k_in), v = packed(v_in);
+  at::Tensor out = at::empty(q.sizes(), q.options());
+  at::Tensor cu = cu_seqlens;
+  if (cu.scalar_type() != at::kInt || !cu.is_contiguous()) cu = cu.to(at::kInt).contiguous();
+  auto view = [](const at::Tensor& t) {
+    vf_tensor4d_t d{};
+    d.data = t.data_ptr();
+    d.size[0] = 1;
+    d.size[1] = t.size(1);
+    d.size[2] = t.size(0);
+    d.size[3] = t.size(2);
+    d.stride[0] = std::max<int64_t>(t.size(0) * t.stride(0), 8);
+    d.stride[1] = t.stride(1);
+    d.stride[2] = t.stride(0);
+    d.stride[3] = t.stride(2);
+    return d;
+  };
+  vf_rpb_attention_args_t a{};
+  a.dtype = dtype_code(q);
+  a.q = view(q);
+  a.k = view(k);
+  a.v = view(v);
+  a.out = view(out);
+  if (rpb_table.has_value()) {
+    const at::Tensor& t = *rpb_table;
+    require_cuda(t, "rpb_table");
+    TORCH_CHECK(t.dim() == 2, "vf_b200: rpb_table must be [num_buckets, heads]");
+    a.rpb_table = t.data_ptr();
+    a.table_rows = t.size(0);
+    a.table_cols = t.size(1);
+    a.table_stride_row = t.stride(0);
+    a.table_stride_col = t.stride(1);
+    a.table_dtype = dtype_code(t);
+  }
+  a.num_buckets = static_cast<int32_t>(num_buckets);
+  a.max_distance = static_cast<int32_t>(max_distance);
+  a.is_decoder = is_decoder ? 1 : 0;
+  a.softmax_scale = static_cast<float>(softmax_scale);
+  TORCH_CHECK(max_seqlen > 0 && max_seqlen <= INT32_MAX, "vf_b200: max_seqlen out of range");
+  check_rc(vf_rpb_attention_varlen_fwd(&a, cu.data_ptr<int32_t>(), static_cast<int32_t>(cu.numel() - 1),
+                                       static_cast<int32_t>(max_seqlen), at::cuda::getCurrentCUDAStream().stream()));
+  return f32 ? out.to(at::kFloat) : out;
+}
+
 at::Tensor deberta_attention(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
                              const std::optional<at::Tensor>& seq_lengths,
                              const std::optional<at::Tensor>& pos_key,
@@ -186,6 +256,15 @@ at::Tensor deberta_attention_meta(const at::Tensor& q, const at::Tensor&, const 
   return at::empty_like(q);
 }
 
+at::Tensor rpb_attention_varlen_meta(const at::Tensor& q, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                     int64_t, const std::optional<at::Tensor>&, int64_t, int64_t, bool, double) {
+  return at::empty_like(q);
+}
+at::Tensor rpb_attention_varlen_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                    int64_t, const std::optional<at::Tensor>&, int64_t, int64_t, bool, double) {
+  TORCH_CHECK(false, "vf_b200: q, k, v must be CUDA tensors (no CPU implementation)");
+}
+
 at::Tensor rpb_attention_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&,
                              const std::optional<at::Tensor>&, int64_t, int64_t, bool,
                              const std::optional<at::Tensor>&, double, double) {
@@ -203,6 +282,8 @@ at::Tensor deberta_attention_cpu(const at::Tensor&, const at::Tensor&, const at:
 TORCH_LIBRARY(vf_b200, m) {
   m.def("rpb_attention(Tensor q, Tensor k, Tensor v, Tensor? rpb_table, int num_buckets, int max_distance, "
         "bool is_decoder, Tensor? padding_mask, float dropout_p, float softmax_scale) -> Tensor");
+  m.def("rpb_attention_varlen(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, int max_seqlen, Tensor? rpb_table, "
+        "int num_buckets, int max_distance, bool is_decoder, float softmax_scale) -> Tensor");
   m.def("deberta_attention(Tensor q, Tensor k, Tensor v, Tensor? seq_lengths, Tensor? pos_key, "
         "Tensor? pos_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "
         "bool use_log_bucket) -> Tensor");
@@ -210,15 +291,18 @@ TORCH_LIBRARY(vf_b200, m) {
 
 TORCH_LIBRARY_IMPL(vf_b200, CUDA, m) {
   m.impl("rpb_attention", &rpb_attention);
+  m.impl("rpb_attention_varlen", &rpb_attention_varlen);
   m.impl("deberta_attention", &deberta_attention);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
   m.impl("rpb_attention", &rpb_attention_cpu);
+  m.impl("rpb_attention_varlen", &rpb_attention_varlen_cpu);
   m.impl("deberta_attention", &deberta_attention_cpu);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
   m.impl("rpb_attention", &rpb_attention_meta);
+  m.impl("rpb_attention_varlen", &rpb_attention_varlen_meta);
   m.impl("deberta_attention", &deberta_attention_meta);
 }

@@ -40,4 +40,28 @@ def flash_attention_rpb_final(
         padding_mask, float(dropout_p), float(softmax_scale))
 
 
-__all__ = ["flash_attention_rpb_final"]
+def flash_attention_rpb_varlen(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    max_seqlen: int,
+    rpb_table: Optional[torch.Tensor],
+    num_buckets: int,
+    max_distance: int,
+    is_decoder: bool = False,
+    softmax_scale: float = 1.0,
+) -> torch.Tensor:
+    """Packed variable-length form (no counterpart in the reference).
+
+    q, k, v: [total, heads, 64], sequence s in rows cu_seqlens[s]:cu_seqlens[s+1]
+    (int32, on the device).  Each sequence attends only within itself, as if it had been
+    padded and passed to `flash_attention_rpb_final` alone with no padding mask; no
+    padding FLOPs are spent.  `max_seqlen` must bound every sequence length.  Returns
+    [total, heads, 64]; rows outside every sequence are left unwritten."""
+    return torch.ops.vf_b200.rpb_attention_varlen(
+        q, k, v, cu_seqlens, int(max_seqlen), rpb_table, int(num_buckets), int(max_distance),
+        bool(is_decoder), float(softmax_scale))
+
+
+__all__ = ["flash_attention_rpb_final", "flash_attention_rpb_varlen"]

@@ -86,6 +86,22 @@ def mt5_attention_inputs(seed: int = 0, device="cuda", B: int = 16, L: int = 768
                 num_buckets=32, max_distance=128)
 
 
+def mt5_varlen_inputs(seed: int = 0, device="cuda", B: int = 16, L: int = 768, H: int = HEADS,
+                      lengths=None, dtype=torch.bfloat16):
+    """C2 in the packed layout: the valid rows of mt5_attention_inputs (same seed, same
+    lengths, same values) back to back as [total, H, 64], with cu_seqlens int32 [B+1]."""
+    w = mt5_attention_inputs(seed=seed, device=device, B=B, L=L, H=H, lengths=lengths, dtype=dtype)
+    lens = [int(x) for x in w["lengths"].tolist()]
+
+    def pack(x):   # (B, H, L, D) -> (total, H, D)
+        return torch.cat([x[b, :, :n].permute(1, 0, 2) for b, n in enumerate(lens)], 0).contiguous()
+
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(lens), 0).tolist()), dtype=torch.int32)
+    return dict(q=pack(w["q"]), k=pack(w["k"]), v=pack(w["v"]), rpb_table=w["rpb_table"],
+                cu_seqlens=cu.to(w["q"].device), max_seqlen=max(lens), lengths=w["lengths"],
+                num_buckets=32, max_distance=128)
+
+
 def deberta_attention_inputs(seed: int = 0, device="cuda", B: int = 8, L: int = 512, H: int = HEADS,
                              lengths=None, dtype=torch.bfloat16, position_buckets: int = 256,
                              max_relative_positions: int = 512, with_positions: bool = True):
