@@ -5,11 +5,14 @@ strides and the current CUDA stream and calls the C ABI of libvf_b200.so:
 
   torch.ops.vf_b200.rpb_attention(q, k, v, rpb_table?, num_buckets, max_distance,
                                   is_decoder, padding_mask?, dropout_p, softmax_scale)
+  torch.ops.vf_b200.rpb_attention_varlen(q, k, v, cu_seqlens, max_seqlen, rpb_table?,
+                                         num_buckets, max_distance, is_decoder,
+                                         softmax_scale)      # packed [total, H, 64]
   torch.ops.vf_b200.deberta_attention(q, k, v, seq_lengths?, pos_key?, pos_query?, causal,
                                       sm_scale?, position_buckets, max_relative_distance,
                                       use_log_bucket)
 
-Both borrow their inputs (layouts TMA cannot describe are copied contiguous), allocate
+All borrow their inputs (layouts TMA cannot describe are copied contiguous), allocate
 only the output, launch on the caller's stream, and have Meta implementations for
 tracing.  CPU tensors raise: there is no CPU implementation.
 """
@@ -30,4 +33,5 @@ if not TORCH_LIB_PATH.exists():
 torch.ops.load_library(str(TORCH_LIB_PATH))
 
 rpb_attention = torch.ops.vf_b200.rpb_attention
+rpb_attention_varlen = torch.ops.vf_b200.rpb_attention_varlen
 deberta_attention = torch.ops.vf_b200.deberta_attention
