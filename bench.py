@@ -146,6 +146,22 @@ def build_workload(name: str, rank: int, device):
                "global_batch": 16, "seq_len": 768, "heads": 16, "head_dim": 64,
                "lengths": "U[256,768] packed, no padding"}
         keys = ("q", "k", "v", "rpb_table", "cu_seqlens")
+    elif name == "deberta_c1_varlen":
+        # C1's sequences packed back to back (cu_seqlens), position rows packed alike.
+        from kernels.flash_deberta_attention import flash_deberta_attention_varlen
+        base = W.deberta_varlen_inputs(seed=2000 + rank, device=device)
+        lens = base["lengths"].tolist()
+        flops = W.core_flops(lens) + W.deberta_pos_flops(lens)
+
+        def call(x):
+            return flash_deberta_attention_varlen(x["q"], x["k"], x["v"], x["cu_seqlens"], x["max_seqlen"],
+                                                  x["pos_key"], x["pos_query"], False, x["sm_scale"], 256, 512, True)
+
+        per_set = sum(base[k].numel() * base[k].element_size() for k in ("q", "k", "v", "pos_key", "pos_query"))
+        cfg = {"workload": "C1 DeBERTa-v3-large disentangled layer (bf16 on GPU), c2p|p2c, 256 buckets, packed (cu_seqlens)",
+               "global_batch": 8, "seq_len": 512, "lengths": "U[64,512] packed, no padding", "heads": 16,
+               "head_dim": 64, "mode": "compat (precomputed pos_key/pos_query)"}
+        keys = ("q", "k", "v", "pos_key", "pos_query", "cu_seqlens")
     elif name.startswith("deberta_c1") or name.startswith("deberta_c5"):
         from kernels.flash_deberta_attention import flash_deberta_attention
         if name == "deberta_c1":

@@ -123,6 +123,20 @@ typedef struct {
 
 int vf_deberta_attention_fwd(const vf_deberta_attention_args_t* args, void* stream);
 
+/* Packed variable-length batch of the same operator (no counterpart in the reference):
+ * sequence s occupies rows [cu_seqlens[s], cu_seqlens[s+1]) of q, k, v, out and of the
+ * position tensors, and attends only within itself, with causal masking (if set) inside
+ * each sequence.  Replaces the pad/unpad loops around kernels/flash_deberta_attention.py:455
+ * in plugins/deberta_gliner/model.py:361-399 and plugins/deberta_gliner_linker/model.py:
+ * 170-228, and the flat-as-one-sequence call of plugins/deberta_gliner2/model.py:125-139.
+ *
+ * q, k, v, out: views of size (1, H, total, 64); pos_key / pos_query: (1, H, total, 2S)
+ * or absent.  seq_lengths must be NULL.  cu_seqlens, num_seqs, max_seqlen: as for
+ * vf_rpb_attention_varlen_fwd (same rules, same error bit).  Rows of out outside every
+ * sequence are not written. */
+int vf_deberta_attention_varlen_fwd(const vf_deberta_attention_args_t* args, const int32_t* cu_seqlens,
+                                    int32_t num_seqs, int32_t max_seqlen, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * Host-side bucket functions (no GPU needed).  These are the exact integer outputs the
  * kernels use; they restate, in float32 arithmetic like the reference's torch code:
@@ -142,7 +156,7 @@ const char* vf_last_error(void);
 
 /* Reads (and optionally clears) the device error word of the current device: bit 0 = a
  * bounded in-kernel wait ran out of time, bit 1 = a gather index failed its bounds check,
- * bit 2 = packed-batch offsets broke the rules of vf_rpb_attention_varlen_fwd.
+ * bit 2 = packed-batch offsets broke the rules of the *_varlen_fwd entry points.
  * Synchronises the device.  Returns the word (>= 0) or VF_ECUDA. */
 int vf_device_error(int32_t clear);
 

@@ -14,7 +14,8 @@ It restates, in plain PyTorch on the CPU, the reference's own algorithms for the
   * DeBERTa bucket:   models/deberta_v2/deberta_v2_encoder.py:70-89 (make_log_bucket_position)
   * DeBERTa op:       kernels/flash_deberta_attention.py:375-448 (_pytorch_flash_deberta_fwd),
                       with the Triton kernel's row semantics (rows >= seq_len are 0,
-                      :295-299, :334)
+                      :295-299, :334); the packed form applies it to each cu_seqlens
+                      sequence alone
   * DeBERTa layer:    models/deberta_v2/deberta_v2_encoder.py:332-487 (_pytorch_forward)
 
 Parity pinning: tests/golden/make_golden.py runs the reference's own functions (imported
@@ -23,6 +24,7 @@ under tests/golden/; tests/test_oracle_golden.py checks this oracle against them
 """
 from .rpb import (  # noqa: F401
     deberta_attention_ref,
+    deberta_attention_varlen_ref,
     deberta_layer_ref,
     deberta_log_bucket_ref,
     rpb_attention_ref,

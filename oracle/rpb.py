@@ -175,6 +175,30 @@ def deberta_attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return out
 
 
+def deberta_attention_varlen_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens,
+                                 pos_key: Optional[torch.Tensor] = None,
+                                 pos_query: Optional[torch.Tensor] = None,
+                                 causal: bool = False, sm_scale: Optional[float] = None,
+                                 position_buckets: int = 0, max_relative_distance: int = 0,
+                                 use_log_bucket: bool = False, dtype=torch.float64,
+                                 fill: float = float("nan")) -> torch.Tensor:
+    """Packed batch: q, k, v [total, H, 64], pos_key / pos_query [total, H, 2S]; sequence s =
+    rows cu_seqlens[s]:cu_seqlens[s+1] is deberta_attention_ref on that sequence alone
+    (every row and key valid: the reference's per-request call, :375-448).  Rows outside
+    every sequence are `fill`."""
+    cu = [int(x) for x in torch.as_tensor(cu_seqlens).tolist()]
+    out = torch.full(q.shape, fill, dtype=dtype)
+    for s in range(len(cu) - 1):
+        a, b = cu[s], cu[s + 1]
+        if b <= a:
+            continue
+        seq = lambda t: None if t is None else t[a:b].permute(1, 0, 2).unsqueeze(0)   # (1, H, L, .)
+        o = deberta_attention_ref(seq(q), seq(k), seq(v), None, seq(pos_key), seq(pos_query), causal, sm_scale,
+                                  position_buckets, max_relative_distance, use_log_bucket, dtype=dtype)
+        out[a:b] = o[0].permute(1, 0, 2)
+    return out
+
+
 def deberta_layer_ref(hidden: torch.Tensor, attention_mask: torch.Tensor,
                       wq: torch.Tensor, bq: torch.Tensor, wk: torch.Tensor, bk: torch.Tensor,
                       wv: torch.Tensor, bv: torch.Tensor, rel_embeddings: torch.Tensor,

@@ -141,3 +141,18 @@ def test_rpb_varlen_validation_rejects_before_launch(mutate, cu, num_seqs, max_s
     rc = lib.vf_rpb_attention_varlen_fwd(ctypes.byref(a), cu, num_seqs, max_seqlen, None)
     assert rc == code
     assert msg in lib.vf_last_error().decode()
+
+
+def test_deberta_varlen_validation_rejects_before_launch():
+    lib = _lib.load()
+    a = _lib.DebertaArgs()
+    a.dtype = _lib.VF_DTYPE_BF16
+    a.q, a.k, a.v, a.out = (_fake_t4((1, 4, 300, 64), 0x10000 * (i + 1)) for i in range(4))
+    a.position_buckets, a.max_relative_distance = 256, 512
+    a.seq_lengths = 0x30000
+    assert lib.vf_deberta_attention_varlen_fwd(ctypes.byref(a), 0x20000, 2, 100, None) == _lib.VF_EUNSUPPORTED
+    assert "seq_lengths" in lib.vf_last_error().decode()
+    a.seq_lengths = None
+    assert lib.vf_deberta_attention_varlen_fwd(ctypes.byref(a), None, 2, 100, None) == _lib.VF_EINVAL
+    assert lib.vf_deberta_attention_varlen_fwd(ctypes.byref(a), 0x20000, 2, 301, None) == _lib.VF_EINVAL
+    assert "max_seqlen" in lib.vf_last_error().decode()

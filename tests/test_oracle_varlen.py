@@ -35,3 +35,22 @@ def test_varlen_oracle_leaves_rows_outside_sequences():
     out = oracle.rpb_attention_varlen_ref(q, q, q, [2, 5, 8], None, 32, 128, False, fill=7.0)
     assert torch.all(out[:2] == 7.0) and torch.all(out[8:] == 7.0)
     assert torch.isfinite(out[2:8]).all() and not torch.any(out[2:8] == 7.0)
+
+
+def test_deberta_varlen_oracle_matches_padded_oracle():
+    """Packed DeBERTa oracle against the padded oracle with seq_lengths (rows past a
+    sequence are 0 there and absent here), log buckets, both position terms, causal too."""
+    g = torch.Generator().manual_seed(4)
+    lens = [1, 40, 129, 0, 200]
+    B, H, L, S = len(lens), 2, max(lens), 32
+    q, k, v = (torch.randn(B, H, L, 64, generator=g) for _ in range(3))
+    pk, pq = (torch.randn(B, H, L, 2 * S, generator=g) for _ in range(2))
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(lens), 0)), dtype=torch.int32)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    for causal in (False, True):
+        pad = oracle.deberta_attention_ref(q, k, v, sl, pk, pq, causal, 0.1, S, 128, True)
+        got = oracle.deberta_attention_varlen_ref(*(_padded_to_packed(t, lens) for t in (q, k, v)), cu,
+                                                  _padded_to_packed(pk, lens), _padded_to_packed(pq, lens),
+                                                  causal, 0.1, S, 128, True)
+        assert_close(got, _padded_to_packed(pad, lens), None, max_abs=1e-9, min_cos=1 - 1e-12,
+                     what=f"deberta causal={causal}")

@@ -184,18 +184,6 @@ template <typename T> struct AbFormat;
 template <> struct AbFormat<__nv_bfloat16> { static constexpr uint32_t value = 1u; };
 template <> struct AbFormat<__half> { static constexpr uint32_t value = 0u; };
 
-// Writes zeros to output rows [r0, r1) of (b, h); used for DeBERTa rows past seq_len.
-template <typename T>
-__device__ void zero_rows(const KParams& p, int b, int h, int r0, int r1, int tid, int nthr) {
-  T* out = reinterpret_cast<T*>(p.out) + b * p.o_sb + h * p.o_sh;
-  const int chunks = (r1 - r0) * (kHeadDim / 8);
-  for (int i = tid; i < chunks; i += nthr) {
-    const int r = r0 + i / (kHeadDim / 8);
-    const int c = (i % (kHeadDim / 8)) * 8;
-    *reinterpret_cast<uint4*>(out + r * p.o_sm + c) = make_uint4(0, 0, 0, 0);
-  }
-}
-
 template <typename M> __device__ __forceinline__ float ld_f(const M* p) { return to_f<M>(p[0]); }
 template <> __device__ __forceinline__ float ld_f<float>(const float* p) { return __ldg(p); }
 
@@ -308,7 +296,7 @@ __device__ __forceinline__ SeqGeo seq_geo(const KParams& p, int b) {
     s.klen = min(max(L, 0), p.N);
     s.qlen = min(max(L, 0), p.M);
   }
-  if (kVariant == kT5 && p.cu_seqlens != nullptr) {
+  if (p.cu_seqlens != nullptr) {
     // Offsets outside [0, packed_rows], decreasing offsets or a sequence longer than
     // max_seqlen set the error word; the rows used are clamped into the views either way.
     const int r0 = __ldg(p.cu_seqlens + b), r1 = __ldg(p.cu_seqlens + b + 1);
@@ -834,18 +822,24 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             }
           }
         } else {
+          // Position rows are rows row0 + m / row0 + n of the views (row0 = 0 unless the batch
+          // is packed, whose single-batch views have their batch strides set to 0 by the host).
+          const int row0 = reinterpret_cast<const volatile int*>(smem + kOffInfo + kOffInfoRow0)[slot];
           const int b = vu->b, h = vu->h, klen = vu->klen;
-          // Position terms.  A missing term (or a row past M) reads one zero element with
-          // stride 0, so the gather loop has no branches and its loads can be in flight
-          // together (a per-column branch around each gather serialised them: ~1.9x
-          // slower).
+          // Position terms.  A missing term (or a row past the sequence, whose output is zero
+          // or not written) reads one zero element with stride 0, so the gather loop has no
+          // branches and its loads can be in flight together (a per-column branch around
+          // each gather serialised them: ~1.9x slower).
           const T* zero = reinterpret_cast<const T*>(&g_zero_pos);
-          const bool pk_on = p.pos_key != nullptr && m < p.M;
-          const T* pk_row = pk_on ? reinterpret_cast<const T*>(p.pos_key) + b * p.pk_sb + h * p.pk_sh + (long long)m * p.pk_sm
+          const bool pk_on = p.pos_key != nullptr && m < vu->qlen;
+          const T* pk_row = pk_on ? reinterpret_cast<const T*>(p.pos_key) + b * p.pk_sb + h * p.pk_sh +
+                                        (long long)(row0 + m) * p.pk_sm
                                   : zero;
           const long long pk_sk = pk_on ? p.pk_sk : 0;
           const bool pq_on = p.pos_query != nullptr;
-          const T* pq_bh = pq_on ? reinterpret_cast<const T*>(p.pos_query) + b * p.pq_sb + h * p.pq_sh : zero;
+          const T* pq_bh = pq_on ? reinterpret_cast<const T*>(p.pos_query) + b * p.pq_sb + h * p.pq_sh +
+                                       (long long)row0 * p.pq_sn
+                                 : zero;
           const long long pq_sn = pq_on ? p.pq_sn : 0, pq_sk = pq_on ? p.pq_sk : 0;
           // S first (one TMEM read, so QK of the next tile can start), then the terms.
           tmem_ld_2x64_f2(tS, x2);
@@ -1310,6 +1304,80 @@ int finish_rpb_table(const vf_rpb_attention_args_t* a, int span, vf::KParams* kp
   return VF_OK;
 }
 
+// Checks shared by the packed-batch entry points (the views and the offsets array).
+int check_packed(const vf_tensor4d_t& q, const vf_tensor4d_t& k, const int32_t* cu_seqlens, int32_t num_seqs,
+                 int32_t max_seqlen, const char* what) {
+  const std::string w(what);
+  if (cu_seqlens == nullptr || (reinterpret_cast<uintptr_t>(cu_seqlens) & 3) != 0)
+    return fail(VF_EINVAL, w + ": cu_seqlens must be a non-null, 4-byte aligned device int32 array");
+  if (num_seqs <= 0 || num_seqs > 65535) return fail(VF_EINVAL, w + ": num_seqs must be in [1, 65535]");
+  if (q.size[0] != 1) return fail(VF_EINVAL, w + ": q/k/v/out must be packed views of size (1, H, total, 64)");
+  if (k.size[2] != q.size[2]) return fail(VF_EINVAL, w + ": k and q must have the same packed rows");
+  if (max_seqlen <= 0 || max_seqlen > q.size[2]) return fail(VF_EINVAL, w + ": max_seqlen must be in [1, total rows]");
+  return VF_OK;
+}
+
+// Shared set-up of the two DeBERTa entry points: operand checks, tensor maps, scale and the
+// position tensors (batch extent `batch`: B, or 1 for a packed batch).  Leaves the causal
+// offset, seq_lengths, the index table and (packed layout) the geometry to the caller.
+int deberta_prepare(const vf_deberta_attention_args_t* a, int64_t batch, vf::KParams* kp) {
+  if (a->dtype != VF_DTYPE_BF16 && a->dtype != VF_DTYPE_F16)
+    return fail(VF_EUNSUPPORTED, "deberta attention: q/k/v dtype must be float16 or bfloat16");
+  int rc = check_qkv(a->q, a->k, a->v, a->out);
+  if (rc) return rc;
+  const int64_t H = a->q.size[1], M = a->q.size[2], N = a->k.size[2];
+  const int span = a->position_buckets > 0 ? a->position_buckets : a->max_relative_distance;
+  const bool has_pos = a->pos_key.data != nullptr || a->pos_query.data != nullptr;
+  if (has_pos && span <= 0) return fail(VF_EINVAL, "deberta attention: position terms need position_buckets or max_relative_distance > 0");
+  std::memset(kp, 0, offsetof(vf::KParams, lut));
+  if ((rc = make_tile_map(&kp->tm_q, a->q, a->dtype, "q"))) return rc;
+  if ((rc = make_tile_map(&kp->tm_k, a->k, a->dtype, "k"))) return rc;
+  if ((rc = make_tile_map(&kp->tm_v, a->v, a->dtype, "v"))) return rc;
+  if ((rc = make_tile_map(&kp->tm_o, a->out, a->dtype, "out"))) return rc;
+  fill_common(kp, a->q, a->k, a->out);
+  const float sm_scale = a->has_sm_scale ? a->sm_scale : 1.0f / std::sqrt(static_cast<float>(vf::kHeadDim));
+  kp->scale_log2 = sm_scale * vf::kLog2e;
+  kp->causal = a->causal ? 1 : 0;
+  kp->span2 = 2 * span;
+  if (a->pos_key.data != nullptr) {
+    const vf_tensor4d_t& t = a->pos_key;
+    if (t.size[0] != batch || t.size[1] != H || t.size[2] != M || t.size[3] < 2 * span)
+      return fail(VF_EINVAL, "deberta attention: pos_key must be (B, H, M, 2*ATT_SPAN)");
+    kp->pos_key = t.data;
+    kp->pk_sb = t.stride[0]; kp->pk_sh = t.stride[1]; kp->pk_sm = t.stride[2]; kp->pk_sk = t.stride[3];
+  }
+  if (a->pos_query.data != nullptr) {
+    const vf_tensor4d_t& t = a->pos_query;
+    if (t.size[0] != batch || t.size[1] != H || t.size[2] != N || t.size[3] < 2 * span)
+      return fail(VF_EINVAL, "deberta attention: pos_query must be (B, H, N, 2*ATT_SPAN)");
+    kp->pos_query = t.data;
+    kp->pq_sb = t.stride[0]; kp->pq_sh = t.stride[1]; kp->pq_sn = t.stride[2]; kp->pq_sk = t.stride[3];
+  }
+  // Log buckets exactly when the reference's torch path uses them
+  // (kernels/flash_deberta_attention.py:400).
+  const bool log_bucket = a->use_log_bucket && a->position_buckets > 0 && a->max_relative_distance > 0;
+  if (log_bucket && (a->position_buckets < 4 || a->max_relative_distance - 1 <= a->position_buckets / 2))
+    return fail(VF_EUNSUPPORTED, "deberta attention: log-bucket configuration outside the formula's domain");
+  return VF_OK;
+}
+
+// Position-index table for relative positions |m - n| < span.
+int finish_deberta_table(const vf_deberta_attention_args_t* a, int span_rows, vf::KParams* kp) {
+  const int span = a->position_buckets > 0 ? a->position_buckets : a->max_relative_distance;
+  const bool has_pos = a->pos_key.data != nullptr || a->pos_query.data != nullptr;
+  const bool log_bucket = a->use_log_bucket && a->position_buckets > 0 && a->max_relative_distance > 0;
+  if (has_pos) {
+    const RelTable& tab = deberta_table(span, a->position_buckets, a->max_relative_distance, log_bucket, span_rows);
+    if (tab.R > vf::kMaxRel) return fail(VF_EUNSUPPORTED, "deberta attention: relative-position table too large");
+    kp->rel_R = tab.R;
+    std::memcpy(kp->lut, tab.lut.data(), tab.lut.size() * sizeof(short));
+  } else {
+    kp->rel_R = 0;
+    kp->lut[0] = 0;
+  }
+  return VF_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1388,17 +1456,12 @@ int vf_rpb_attention_fwd(const vf_rpb_attention_args_t* a, void* stream) {
 int vf_rpb_attention_varlen_fwd(const vf_rpb_attention_args_t* a, const int32_t* cu_seqlens, int32_t num_seqs,
                                 int32_t max_seqlen, void* stream) {
   if (a == nullptr) return fail(VF_EINVAL, "null args");
-  if (cu_seqlens == nullptr || (reinterpret_cast<uintptr_t>(cu_seqlens) & 3) != 0)
-    return fail(VF_EINVAL, "rpb varlen: cu_seqlens must be a non-null, 4-byte aligned device int32 array");
-  if (num_seqs <= 0 || num_seqs > 65535) return fail(VF_EINVAL, "rpb varlen: num_seqs must be in [1, 65535]");
-  if (a->q.size[0] != 1) return fail(VF_EINVAL, "rpb varlen: q/k/v/out must be packed views of size (1, H, total, 64)");
-  if (a->k.size[2] != a->q.size[2]) return fail(VF_EINVAL, "rpb varlen: k and q must have the same packed rows");
+  int rc = check_packed(a->q, a->k, cu_seqlens, num_seqs, max_seqlen, "rpb varlen");
+  if (rc) return rc;
   if (a->padding_mask.data != nullptr)
     return fail(VF_EUNSUPPORTED, "rpb varlen: the packed layout takes no padding_mask (sequences are exact)");
-  if (max_seqlen <= 0 || max_seqlen > a->q.size[2])
-    return fail(VF_EINVAL, "rpb varlen: max_seqlen must be in [1, total rows]");
   static thread_local vf::KParams kp;
-  int rc = rpb_prepare(a, &kp);
+  rc = rpb_prepare(a, &kp);
   if (rc) return rc;
   kp.cu_seqlens = cu_seqlens;
   kp.packed_rows = kp.M;
@@ -1411,58 +1474,33 @@ int vf_rpb_attention_varlen_fwd(const vf_rpb_attention_args_t* a, const int32_t*
 
 int vf_deberta_attention_fwd(const vf_deberta_attention_args_t* a, void* stream) {
   if (a == nullptr) return fail(VF_EINVAL, "null args");
-  if (a->dtype != VF_DTYPE_BF16 && a->dtype != VF_DTYPE_F16)
-    return fail(VF_EUNSUPPORTED, "deberta attention: q/k/v dtype must be float16 or bfloat16");
-  int rc = check_qkv(a->q, a->k, a->v, a->out);
-  if (rc) return rc;
-  const int B = static_cast<int>(a->q.size[0]), H = static_cast<int>(a->q.size[1]);
-  const int M = static_cast<int>(a->q.size[2]), N = static_cast<int>(a->k.size[2]);
-  const int span = a->position_buckets > 0 ? a->position_buckets : a->max_relative_distance;
-  const bool has_pos = a->pos_key.data != nullptr || a->pos_query.data != nullptr;
-  if (has_pos && span <= 0) return fail(VF_EINVAL, "deberta attention: position terms need position_buckets or max_relative_distance > 0");
   static thread_local vf::KParams kp;
-  std::memset(&kp, 0, offsetof(vf::KParams, lut));
-  if ((rc = make_tile_map(&kp.tm_q, a->q, a->dtype, "q"))) return rc;
-  if ((rc = make_tile_map(&kp.tm_k, a->k, a->dtype, "k"))) return rc;
-  if ((rc = make_tile_map(&kp.tm_v, a->v, a->dtype, "v"))) return rc;
-  if ((rc = make_tile_map(&kp.tm_o, a->out, a->dtype, "out"))) return rc;
-  fill_common(&kp, a->q, a->k, a->out);
-  const float sm_scale = a->has_sm_scale ? a->sm_scale : 1.0f / std::sqrt(static_cast<float>(vf::kHeadDim));
-  kp.scale_log2 = sm_scale * vf::kLog2e;
-  kp.causal = a->causal ? 1 : 0;
+  int rc = deberta_prepare(a, a->q.size[0], &kp);
+  if (rc) return rc;
+  const int M = kp.M, N = kp.N;
   kp.p_seq = N - M;
   kp.seq_lengths = a->seq_lengths;
-  kp.span2 = 2 * span;
-  if (a->pos_key.data != nullptr) {
-    const vf_tensor4d_t& t = a->pos_key;
-    if (t.size[0] != B || t.size[1] != H || t.size[2] != M || t.size[3] < 2 * span)
-      return fail(VF_EINVAL, "deberta attention: pos_key must be (B, H, M, 2*ATT_SPAN)");
-    kp.pos_key = t.data;
-    kp.pk_sb = t.stride[0]; kp.pk_sh = t.stride[1]; kp.pk_sm = t.stride[2]; kp.pk_sk = t.stride[3];
+  if ((rc = finish_deberta_table(a, std::max(M, N), &kp))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return a->dtype == VF_DTYPE_BF16 ? launch<vf::kDeberta, __nv_bfloat16>(&kp, s) : launch<vf::kDeberta, __half>(&kp, s);
+}
 
-  }
-  if (a->pos_query.data != nullptr) {
-    const vf_tensor4d_t& t = a->pos_query;
-    if (t.size[0] != B || t.size[1] != H || t.size[2] != N || t.size[3] < 2 * span)
-      return fail(VF_EINVAL, "deberta attention: pos_query must be (B, H, N, 2*ATT_SPAN)");
-    kp.pos_query = t.data;
-    kp.pq_sb = t.stride[0]; kp.pq_sh = t.stride[1]; kp.pq_sn = t.stride[2]; kp.pq_sk = t.stride[3];
-
-  }
-  // Log buckets exactly when the reference's torch path uses them
-  // (kernels/flash_deberta_attention.py:400).
-  const bool log_bucket = a->use_log_bucket && a->position_buckets > 0 && a->max_relative_distance > 0;
-  if (log_bucket && (a->position_buckets < 4 || a->max_relative_distance - 1 <= a->position_buckets / 2))
-    return fail(VF_EUNSUPPORTED, "deberta attention: log-bucket configuration outside the formula's domain");
-  if (has_pos) {
-    const RelTable& tab = deberta_table(span, a->position_buckets, a->max_relative_distance, log_bucket, std::max(M, N));
-    if (tab.R > vf::kMaxRel) return fail(VF_EUNSUPPORTED, "deberta attention: relative-position table too large");
-    kp.rel_R = tab.R;
-    std::memcpy(kp.lut, tab.lut.data(), tab.lut.size() * sizeof(short));
-  } else {
-    kp.rel_R = 0;
-    kp.lut[0] = 0;
-  }
+int vf_deberta_attention_varlen_fwd(const vf_deberta_attention_args_t* a, const int32_t* cu_seqlens,
+                                    int32_t num_seqs, int32_t max_seqlen, void* stream) {
+  if (a == nullptr) return fail(VF_EINVAL, "null args");
+  int rc = check_packed(a->q, a->k, cu_seqlens, num_seqs, max_seqlen, "deberta varlen");
+  if (rc) return rc;
+  if (a->seq_lengths != nullptr)
+    return fail(VF_EUNSUPPORTED, "deberta varlen: seq_lengths must be NULL (cu_seqlens gives the lengths)");
+  static thread_local vf::KParams kp;
+  if ((rc = deberta_prepare(a, 1, &kp))) return rc;
+  kp.cu_seqlens = cu_seqlens;
+  kp.packed_rows = kp.M;
+  kp.B = num_seqs;
+  kp.M = kp.N = max_seqlen;
+  kp.p_seq = 0;
+  kp.pk_sb = kp.pq_sb = 0;   // one packed batch: the kernel's batch coordinate is 0
+  if ((rc = finish_deberta_table(a, max_seqlen, &kp))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return a->dtype == VF_DTYPE_BF16 ? launch<vf::kDeberta, __nv_bfloat16>(&kp, s) : launch<vf::kDeberta, __half>(&kp, s);
 }

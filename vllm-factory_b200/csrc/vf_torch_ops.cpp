@@ -122,6 +122,39 @@ at::Tensor rpb_attention(const at::Tensor& q_in, const at::Tensor& k_in, const a
   return f32 ? out.to(at::kFloat) : out;
 }
 
+// Packed batches: [total, H, D] tensors seen by the kernels as (1, H, total, D) views.
+vf_tensor4d_t packed_view(const at::Tensor& t) {
+  vf_tensor4d_t d{};
+  d.data = t.data_ptr();
+  d.size[0] = 1;
+  d.size[1] = t.size(1);
+  d.size[2] = t.size(0);
+  d.size[3] = t.size(2);
+  d.stride[0] = std::max<int64_t>(t.size(0) * t.stride(0), 8);
+  d.stride[1] = t.stride(1);
+  d.stride[2] = t.stride(0);
+  d.stride[3] = t.stride(2);
+  return d;
+}
+
+// Kernel dtype, unit innermost stride, 16-byte aligned base and row / head strides (TMA).
+at::Tensor packed_tma_ready(const at::Tensor& t) {
+  at::Tensor x = to_kernel_dtype(t);
+  const int64_t es = x.element_size();
+  if (x.stride(2) != 1 || (x.stride(0) * es) % 16 != 0 || (x.stride(1) * es) % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) != 0)
+    x = x.contiguous();
+  return x;
+}
+
+at::Tensor cu_int32(const at::Tensor& cu_seqlens) {
+  require_cuda(cu_seqlens, "cu_seqlens");
+  TORCH_CHECK(cu_seqlens.dim() == 1 && cu_seqlens.numel() >= 2, "vf_b200: cu_seqlens must be [num_seqs + 1]");
+  at::Tensor cu = cu_seqlens;
+  if (cu.scalar_type() != at::kInt || !cu.is_contiguous()) cu = cu.to(at::kInt).contiguous();
+  return cu;
+}
+
 // Packed batch: q, k, v are [total, H, 64] (the rows of every sequence back to back),
 // cu_seqlens int32 [num_seqs + 1]; the kernel sees them as (1, H, total, 64) views.
 at::Tensor rpb_attention_varlen(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
@@ -131,44 +164,20 @@ at::Tensor rpb_attention_varlen(const at::Tensor& q_in, const at::Tensor& k_in, 
   require_cuda(q_in, "q");
   require_cuda(k_in, "k");
   require_cuda(v_in, "v");
-  require_cuda(cu_seqlens, "cu_seqlens");
   TORCH_CHECK(q_in.dim() == 3 && k_in.dim() == 3 && v_in.dim() == 3, "vf_b200: packed q, k, v must be [total, heads, 64]");
   TORCH_CHECK(q_in.scalar_type() == k_in.scalar_type() && q_in.scalar_type() == v_in.scalar_type(),
               "vf_b200: q, k, v must share a dtype");
-  TORCH_CHECK(cu_seqlens.dim() == 1 && cu_seqlens.numel() >= 2, "vf_b200: cu_seqlens must be [num_seqs + 1]");
   c10::cuda::CUDAGuard guard(q_in.device());
   const bool f32 = q_in.scalar_type() == at::kFloat;
-  // (total, H, D) -> (1, H, total, D) views; TMA wants unit innermost stride and 16-byte rows.
-  auto packed = [](const at::Tensor& t) {
-    at::Tensor x = to_kernel_dtype(t);
-    if (x.stride(2) != 1 || (x.stride(0) * x.element_size()) % 16 != 0 || (x.stride(1) * x.element_size()) % 16 != 0 ||
-        (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) != 0)
-      x = x.contiguous();
-    return x;
-  };
-  const at::Tensor q = packed(q_in), k = packed(k_in), v = packed(v_in);
+  const at::Tensor q = packed_tma_ready(q_in), k = packed_tma_ready(k_in), v = packed_tma_ready(v_in);
   at::Tensor out = at::empty(q.sizes(), q.options());
-  at::Tensor cu = cu_seqlens;
-  if (cu.scalar_type() != at::kInt || !cu.is_contiguous()) cu = cu.to(at::kInt).contiguous();
-  auto view = [](const at::Tensor& t) {
-    vf_tensor4d_t d{};
-    d.data = t.data_ptr();
-    d.size[0] = 1;
-    d.size[1] = t.size(1);
-    d.size[2] = t.size(0);
-    d.size[3] = t.size(2);
-    d.stride[0] = std::max<int64_t>(t.size(0) * t.stride(0), 8);
-    d.stride[1] = t.stride(1);
-    d.stride[2] = t.stride(0);
-    d.stride[3] = t.stride(2);
-    return d;
-  };
+  const at::Tensor cu = cu_int32(cu_seqlens);
   vf_rpb_attention_args_t a{};
   a.dtype = dtype_code(q);
-  a.q = view(q);
-  a.k = view(k);
-  a.v = view(v);
-  a.out = view(out);
+  a.q = packed_view(q);
+  a.k = packed_view(k);
+  a.v = packed_view(v);
+  a.out = packed_view(out);
   if (rpb_table.has_value()) {
     const at::Tensor& t = *rpb_table;
     require_cuda(t, "rpb_table");
@@ -243,6 +252,57 @@ at::Tensor deberta_attention(const at::Tensor& q_in, const at::Tensor& k_in, con
   return f32 ? out.to(at::kFloat) : out;
 }
 
+// Packed DeBERTa batch: q, k, v [total, H, 64]; pos_key / pos_query [total, H, 2S].
+at::Tensor deberta_attention_varlen(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
+                                    const at::Tensor& cu_seqlens, int64_t max_seqlen,
+                                    const std::optional<at::Tensor>& pos_key,
+                                    const std::optional<at::Tensor>& pos_query, bool causal,
+                                    std::optional<double> sm_scale, int64_t position_buckets,
+                                    int64_t max_relative_distance, bool use_log_bucket) {
+  require_cuda(q_in, "q");
+  require_cuda(k_in, "k");
+  require_cuda(v_in, "v");
+  TORCH_CHECK(q_in.dim() == 3 && k_in.dim() == 3 && v_in.dim() == 3, "vf_b200: packed q, k, v must be [total, heads, 64]");
+  TORCH_CHECK(q_in.scalar_type() == k_in.scalar_type() && q_in.scalar_type() == v_in.scalar_type(),
+              "vf_b200: q, k, v must share a dtype");
+  c10::cuda::CUDAGuard guard(q_in.device());
+  const bool f32 = q_in.scalar_type() == at::kFloat;
+  const at::Tensor q = packed_tma_ready(q_in), k = packed_tma_ready(k_in), v = packed_tma_ready(v_in);
+  at::Tensor out = at::empty(q.sizes(), q.options());
+  const at::Tensor cu = cu_int32(cu_seqlens);
+  vf_deberta_attention_args_t a{};
+  a.dtype = dtype_code(q);
+  a.q = packed_view(q);
+  a.k = packed_view(k);
+  a.v = packed_view(v);
+  a.out = packed_view(out);
+  at::Tensor pk, pq;   // kernel-dtype copies stay alive until the launch is enqueued
+  if (pos_key.has_value()) {
+    require_cuda(*pos_key, "pos_key");
+    TORCH_CHECK(pos_key->dim() == 3, "vf_b200: packed pos_key must be [total, heads, 2*span]");
+    TORCH_CHECK(pos_key->scalar_type() == q_in.scalar_type(), "vf_b200: pos_key must have the dtype of q");
+    pk = to_kernel_dtype(*pos_key);
+    a.pos_key = packed_view(pk);
+  }
+  if (pos_query.has_value()) {
+    require_cuda(*pos_query, "pos_query");
+    TORCH_CHECK(pos_query->dim() == 3, "vf_b200: packed pos_query must be [total, heads, 2*span]");
+    TORCH_CHECK(pos_query->scalar_type() == q_in.scalar_type(), "vf_b200: pos_query must have the dtype of q");
+    pq = to_kernel_dtype(*pos_query);
+    a.pos_query = packed_view(pq);
+  }
+  a.causal = causal ? 1 : 0;
+  a.has_sm_scale = sm_scale.has_value() ? 1 : 0;
+  a.sm_scale = sm_scale.has_value() ? static_cast<float>(*sm_scale) : 0.f;
+  a.position_buckets = static_cast<int32_t>(position_buckets);
+  a.max_relative_distance = static_cast<int32_t>(max_relative_distance);
+  a.use_log_bucket = use_log_bucket ? 1 : 0;
+  TORCH_CHECK(max_seqlen > 0 && max_seqlen <= INT32_MAX, "vf_b200: max_seqlen out of range");
+  check_rc(vf_deberta_attention_varlen_fwd(&a, cu.data_ptr<int32_t>(), static_cast<int32_t>(cu.numel() - 1),
+                                           static_cast<int32_t>(max_seqlen), at::cuda::getCurrentCUDAStream().stream()));
+  return f32 ? out.to(at::kFloat) : out;
+}
+
 // Shape functions for tracing (torch.compile / fake tensors).
 at::Tensor rpb_attention_meta(const at::Tensor& q, const at::Tensor&, const at::Tensor&,
                               const std::optional<at::Tensor>&, int64_t, int64_t, bool,
@@ -262,6 +322,17 @@ at::Tensor rpb_attention_varlen_meta(const at::Tensor& q, const at::Tensor&, con
 }
 at::Tensor rpb_attention_varlen_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
                                     int64_t, const std::optional<at::Tensor>&, int64_t, int64_t, bool, double) {
+  TORCH_CHECK(false, "vf_b200: q, k, v must be CUDA tensors (no CPU implementation)");
+}
+
+at::Tensor deberta_attention_varlen_meta(const at::Tensor& q, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                         int64_t, const std::optional<at::Tensor>&, const std::optional<at::Tensor>&,
+                                         bool, std::optional<double>, int64_t, int64_t, bool) {
+  return at::empty_like(q);
+}
+at::Tensor deberta_attention_varlen_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                        int64_t, const std::optional<at::Tensor>&, const std::optional<at::Tensor>&,
+                                        bool, std::optional<double>, int64_t, int64_t, bool) {
   TORCH_CHECK(false, "vf_b200: q, k, v must be CUDA tensors (no CPU implementation)");
 }
 
@@ -287,22 +358,28 @@ TORCH_LIBRARY(vf_b200, m) {
   m.def("deberta_attention(Tensor q, Tensor k, Tensor v, Tensor? seq_lengths, Tensor? pos_key, "
         "Tensor? pos_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "
         "bool use_log_bucket) -> Tensor");
+  m.def("deberta_attention_varlen(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, int max_seqlen, Tensor? pos_key, "
+        "Tensor? pos_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "
+        "bool use_log_bucket) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, CUDA, m) {
   m.impl("rpb_attention", &rpb_attention);
   m.impl("rpb_attention_varlen", &rpb_attention_varlen);
   m.impl("deberta_attention", &deberta_attention);
+  m.impl("deberta_attention_varlen", &deberta_attention_varlen);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
   m.impl("rpb_attention", &rpb_attention_cpu);
   m.impl("rpb_attention_varlen", &rpb_attention_varlen_cpu);
   m.impl("deberta_attention", &deberta_attention_cpu);
+  m.impl("deberta_attention_varlen", &deberta_attention_varlen_cpu);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
   m.impl("rpb_attention", &rpb_attention_meta);
   m.impl("rpb_attention_varlen", &rpb_attention_varlen_meta);
   m.impl("deberta_attention", &deberta_attention_meta);
+  m.impl("deberta_attention_varlen", &deberta_attention_varlen_meta);
 }

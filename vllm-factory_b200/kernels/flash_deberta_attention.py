@@ -44,10 +44,38 @@ def flash_deberta_attention(
         int(position_buckets), int(max_relative_distance), bool(use_log_bucket))
 
 
+def flash_deberta_attention_varlen(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cu_seqlens: torch.Tensor,
+    max_seqlen: int,
+    pos_key: Optional[torch.Tensor] = None,
+    pos_query: Optional[torch.Tensor] = None,
+    causal: bool = False,
+    sm_scale: Optional[float] = None,
+    position_buckets: int = 0,
+    max_relative_distance: int = 0,
+    use_log_bucket: bool = False,
+) -> torch.Tensor:
+    """Packed variable-length form (no counterpart in the reference).
+
+    q, k, v: [total, heads, 64]; pos_key / pos_query: [total, heads, 2S] (the per-row
+    position scores of the packed rows) or None.  Sequence s is rows
+    cu_seqlens[s]:cu_seqlens[s+1] (int32, on the device) and attends only within itself,
+    as if it had been passed alone to `flash_deberta_attention` with seq_lengths = its
+    length.  `max_seqlen` must bound every sequence length.  Returns [total, heads, 64];
+    rows outside every sequence are left unwritten."""
+    return torch.ops.vf_b200.deberta_attention_varlen(
+        q, k, v, cu_seqlens, int(max_seqlen), pos_key, pos_query, bool(causal),
+        None if sm_scale is None else float(sm_scale),
+        int(position_buckets), int(max_relative_distance), bool(use_log_bucket))
+
+
 def clear_config_cache() -> None:
     """Reference API (kernels/flash_deberta_attention.py:502).  The reference cached Triton
     tile configurations; this implementation has a single configuration, so there is
     nothing to clear."""
 
 
-__all__ = ["flash_deberta_attention", "clear_config_cache", "HAS_TRITON"]
+__all__ = ["flash_deberta_attention", "flash_deberta_attention_varlen", "clear_config_cache", "HAS_TRITON"]

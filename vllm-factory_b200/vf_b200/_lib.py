@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "vf_rpb_attention_fwd",
     "vf_rpb_attention_varlen_fwd",
     "vf_deberta_attention_fwd",
+    "vf_deberta_attention_varlen_fwd",
     "vf_t5_relative_bucket",
     "vf_deberta_log_bucket",
     "vf_last_error",
@@ -121,6 +122,9 @@ def load() -> ctypes.CDLL:
         lib.vf_rpb_attention_varlen_fwd.restype = ctypes.c_int
         lib.vf_deberta_attention_fwd.argtypes = [ctypes.POINTER(DebertaArgs), ctypes.c_void_p]
         lib.vf_deberta_attention_fwd.restype = ctypes.c_int
+        lib.vf_deberta_attention_varlen_fwd.argtypes = [ctypes.POINTER(DebertaArgs), ctypes.c_void_p,
+                                                        ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
+        lib.vf_deberta_attention_varlen_fwd.restype = ctypes.c_int
         lib.vf_t5_relative_bucket.argtypes = [ctypes.c_int32] * 5 + [ctypes.POINTER(ctypes.c_int32)]
         lib.vf_t5_relative_bucket.restype = ctypes.c_int
         lib.vf_deberta_log_bucket.argtypes = [ctypes.c_int32] * 4 + [ctypes.POINTER(ctypes.c_int32)]

@@ -11,6 +11,9 @@ strides and the current CUDA stream and calls the C ABI of libvf_b200.so:
   torch.ops.vf_b200.deberta_attention(q, k, v, seq_lengths?, pos_key?, pos_query?, causal,
                                       sm_scale?, position_buckets, max_relative_distance,
                                       use_log_bucket)
+  torch.ops.vf_b200.deberta_attention_varlen(q, k, v, cu_seqlens, max_seqlen, pos_key?,
+                                             pos_query?, causal, sm_scale?, position_buckets,
+                                             max_relative_distance, use_log_bucket)   # packed
 
 All borrow their inputs (layouts TMA cannot describe are copied contiguous), allocate
 only the output, launch on the caller's stream, and have Meta implementations for
@@ -35,3 +38,4 @@ torch.ops.load_library(str(TORCH_LIB_PATH))
 rpb_attention = torch.ops.vf_b200.rpb_attention
 rpb_attention_varlen = torch.ops.vf_b200.rpb_attention_varlen
 deberta_attention = torch.ops.vf_b200.deberta_attention
+deberta_attention_varlen = torch.ops.vf_b200.deberta_attention_varlen

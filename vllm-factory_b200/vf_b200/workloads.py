@@ -134,3 +134,21 @@ def deberta_attention_inputs(seed: int = 0, device="cuda", B: int = 8, L: int = 
         out["rel_key"] = kr
         out["rel_query"] = qr
     return out
+
+
+def deberta_varlen_inputs(seed: int = 0, device="cuda", B: int = 8, L: int = 512, H: int = HEADS,
+                          lengths=None, dtype=torch.bfloat16):
+    """C1 in the packed layout: the valid rows of deberta_attention_inputs (same seed, same
+    values) back to back: q, k, v [total, H, 64], pos_key / pos_query [total, H, 2S], with
+    cu_seqlens int32 [B+1]."""
+    w = deberta_attention_inputs(seed=seed, device=device, B=B, L=L, H=H, lengths=lengths, dtype=dtype)
+    lens = [int(x) for x in w["lengths"].tolist()]
+
+    def pack(x):   # (B, H, L, X) -> (total, H, X)
+        return torch.cat([x[b, :, :n].permute(1, 0, 2) for b, n in enumerate(lens)], 0).contiguous()
+
+    cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(lens), 0).tolist()), dtype=torch.int32)
+    out = {k: w[k] for k in ("lengths", "sm_scale", "position_buckets", "max_relative_distance", "use_log_bucket")}
+    out.update(q=pack(w["q"]), k=pack(w["k"]), v=pack(w["v"]), pos_key=pack(w["pos_key"]),
+               pos_query=pack(w["pos_query"]), cu_seqlens=cu.to(w["q"].device), max_seqlen=max(lens))
+    return out
