@@ -18,6 +18,11 @@ Multi-GPU (torchrun, one process per GPU): every rank runs its own 16-sequence s
 (independent sequences, weak scaling); NCCL is used only for the barrier and to take the
 max time over ranks.  `--impl reference` times the reference's CPU implementation (the
 oracle port) on rank 0 and prints the same metric.
+
+Other workloads (`--workload`): deberta_c1 / deberta_c1_fp32 / deberta_c5_<L> (DeBERTa
+attention), mt5_c2_varlen / deberta_c1_varlen (packed batches), and the encoder stacks
+deberta_c3 / mt5_c4: a 256-sequence packed batch partitioned by sequence over the ranks
+(LPT on estimated FLOPs, strong scaling), 24 layers per step, value = encoder tokens/s.
 """
 from __future__ import annotations
 
@@ -242,6 +247,140 @@ def cpu_baseline(name: str, lens, budget_s: float = 12.0):
     return {"value": flops_done / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
 
 
+# ----------------------------------------------------------------------------- encoder stacks
+ENCODER_WORKLOADS = ("deberta_c3", "mt5_c4")
+
+
+def encoder_setup(name: str):
+    """(model class, config, lengths, ids, attention FLOPs per layer of one sequence)."""
+    from vf_b200 import encoders as EN
+    from vf_b200 import workloads as W
+    if name == "deberta_c3":
+        cfg = EN.DebertaConfig()
+        lengths, ids = EN.packed_batch(256, 128, 768, cfg.vocab, seed=0)
+        attn = lambda L: W.core_flops([L]) + W.deberta_pos_flops([L])
+        return EN.DebertaV3Encoder, cfg, lengths, ids, attn
+    cfg = EN.MT5Config()
+    lengths, ids = EN.packed_batch(256, 512, 768, cfg.vocab, seed=0)
+    return EN.MT5Encoder, cfg, lengths, ids, lambda L: W.core_flops([L])
+
+
+def encoder_cpu_baseline(name: str, budget_s: float = 15.0):
+    """The stack's layers on the host cores (fp32, the oracle's attention), on the first
+    sequences of the batch, 2 layers: encoder tokens/s per layer, as a reported baseline."""
+    import dataclasses
+
+    import oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    cls, cfg, lengths, ids, _ = encoder_setup(name)
+    from vf_b200 import encoders as EN
+    small = dataclasses.replace(cfg, layers=2)
+    if name == "deberta_c3":
+        fn = lambda q, k, v, cu, ms, pk, pq, c, sm, pb, mr, lg: oracle.deberta_attention_varlen_ref(
+            q, k, v, cu, pk, pq, c, sm, pb, mr, lg, dtype=torch.float32)
+    else:
+        fn = lambda q, k, v, cu, ms, t, nb, md, dec, sc: oracle.rpb_attention_varlen_ref(
+            q, k, v, cu, t, nb, md, dec, sc, dtype=torch.float32)
+    model = cls(small, device="cpu", dtype=torch.float32, seed=0, attention_fn=fn)
+    done, n, t0 = 0, 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s and n < len(lengths):
+        x, cu, lens = EN.select_sequences(lengths, ids, [n])
+        model.forward(x, cu, lens[0])
+        done += lens[0]
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": done * small.layers / dt, "unit": "tokens/s per layer", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"first {n} sequences, 2 layers, fp32 torch on CPU with the oracle's attention"}
+
+
+def run_encoder(args, world: int, rank: int, dev, warmup: int):
+    """C3 / C4: the 256-sequence packed batch is partitioned by sequence over the ranks
+    (LPT on estimated FLOPs), each rank runs the 24-layer stack on its shard; value =
+    encoder tokens/s of the whole job (total valid tokens / max rank time)."""
+    from vf_b200 import dist as VD
+    from vf_b200 import encoders as EN
+    cls, cfg, lengths, ids, attn = encoder_setup(args.workload)
+    model = cls(cfg, device=dev, seed=0)
+    gemm_tok = model.flops_per_token_gemm()
+    costs = [gemm_tok * int(L) + cfg.layers * attn(int(L)) for L in lengths.tolist()]
+    mine = VD.lpt_shard(costs, world)[rank]
+    x_ids, cu, lens = EN.select_sequences(lengths, ids, mine)
+    x_dev, cu_dev, max_len = x_ids.to(dev), cu.to(dev), max(lens)
+    flops = sum(costs[i] for i in mine)
+    tokens = float(sum(lens))
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(warmup):
+        model.forward(x_dev, cu_dev, max_len)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dev.index or 0)
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        model.forward(x_dev, cu_dev, max_len)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    ms_max, flops_all, tokens_all = VD.reduce_timing(ms, flops, tokens, dev)
+    value = tokens_all * args.steps / (ms_max * 1e-3)
+
+    e2e = None
+    if not args.no_e2e:
+        ids_host, cu_host = x_ids.pin_memory(), cu.pin_memory()
+        out_host = torch.empty((x_ids.shape[0], cfg.hidden), dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            o = model.forward(ids_host.to(dev, non_blocking=True), cu_host.to(dev, non_blocking=True), max_len)
+            out_host.copy_(o, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(3, min(args.steps, 10))
+        e0.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ems, _, _ = VD.reduce_timing(e0.elapsed_time(e1), 0.0, 0.0, dev)
+        e2e = {"value": tokens_all * n_e2e / (ems * 1e-3), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(ids_host.numel() * ids_host.element_size() + cu_host.numel() * 4),
+               "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()), "steps": n_e2e}
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    achieved = flops / (ms / args.steps * 1e-3) / 1e12
+    name = {"deberta_c3": "C3 DeBERTa-v3-large 24-layer encoder stack", "mt5_c4": "C4 mT5-large 24-layer encoder stack"}
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": name[args.workload], "sequences": int(len(lengths)),
+                       "tokens": int(lengths.sum()), "layers": cfg.layers,
+                       "lengths": "U[128,768]" if args.workload == "deberta_c3" else "U[512,768]",
+                       "partition": "packed batch, LPT by estimated FLOPs over ranks",
+                       "l2": "weights (>0.8 GB) and activations exceed L2; no flush"},
+            "attention_flops_share": sum(cfg.layers * attn(int(lengths[i])) for i in mine) / flops,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
+                         "frac": achieved / peaks["bf16"], "traffic": None,
+                         "peak_source": f"{peaks['source']} bf16 dense (burst)",
+                         "what": "whole stack: GEMM + attention algorithmic FLOPs of rank 0's shard per second"},
+            "gpu_launches": args.steps * cfg.layers, "clocks": clocks, "e2e": e2e}
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = encoder_cpu_baseline(args.workload)
+    return line
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -262,13 +401,16 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        cb = cpu_baseline(args.workload, None, budget_s=max(5.0, min(60.0, 2.0 * args.steps)))
-        line = {"metric": METRIC, "value": cb["value"], "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+        if args.workload in ENCODER_WORKLOADS:
+            cb = encoder_cpu_baseline(args.workload)
+        else:
+            cb = cpu_baseline(args.workload, None, budget_s=max(5.0, min(60.0, 2.0 * args.steps)))
+        line = {"metric": METRIC, "value": cb["value"], "unit": cb["unit"], "n_gpus": args.gpus, "steps": args.steps,
                 "warmup": warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic", "impl": "reference",
                 "config": {"workload": args.workload},
                 "cpu_baseline": cb,
-                "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+                "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
         return
 
@@ -283,6 +425,14 @@ def main():
                                              device_id=dev)
     import vf_b200
     vf_b200.load()
+
+    if args.workload in ENCODER_WORKLOADS:
+        line = run_encoder(args, world, rank, dev, warmup)
+        if line is not None:
+            print(json.dumps(line))
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
 
     sets, call, flops, tokens, cfg, keys, lens = build_workload(args.workload, rank, dev)
     stream = torch.cuda.current_stream(dev)

@@ -1,0 +1,47 @@
+"""Encoder stacks on the GPU: the packed attention ops inside 2-layer C3 / C4 stacks (full
+widths) against the same stacks with the oracle's attention (CPU, fp64, cast back) in place
+of the op, so the bf16 GEMMs are shared and only the attention differs."""
+import dataclasses
+
+import pytest
+import torch
+
+import oracle
+from _util import assert_close
+from vf_b200 import encoders as EN
+
+pytestmark = pytest.mark.gpu
+
+
+def _deb_ref(q, k, v, cu, ms, pk, pq, c, sm, pb, mr, lg):
+    f = lambda t: t.float().cpu()
+    o = oracle.deberta_attention_varlen_ref(f(q), f(k), f(v), cu.cpu(), f(pk), f(pq), c, sm, pb, mr, lg)
+    return o.to(q.dtype).to(q.device)
+
+
+def _t5_ref(q, k, v, cu, ms, t, nb, md, dec, sc):
+    f = lambda x: x.float().cpu()
+    o = oracle.rpb_attention_varlen_ref(f(q), f(k), f(v), cu.cpu(), f(t), nb, md, dec, sc)
+    return o.to(q.dtype).to(q.device)
+
+
+def _compare(cls, cfg, ref_fn, lo, hi, what):
+    lengths, ids = EN.packed_batch(5, lo, hi, cfg.vocab, seed=3)
+    x, cu, lens = EN.select_sequences(lengths, ids, range(5))
+    x, cu = x.cuda(), cu.cuda()
+    ours = cls(cfg, device="cuda", seed=0).forward(x, cu, max(lens))
+    ref = cls(cfg, device="cuda", seed=0, attention_fn=ref_fn).forward(x, cu, max(lens))
+    torch.cuda.synchronize()
+    assert torch.isfinite(ours.float()).all()
+    err, cos = assert_close(ours, ref.float(), None, max_abs=0.1, min_cos=0.999, what=what)
+    print(f"{what}: max_abs {err:.3e} min_cos {cos:.6f}")
+
+
+def test_deberta_c3_stack_two_layers():
+    cfg = dataclasses.replace(EN.DebertaConfig(), layers=2, vocab=4000)
+    _compare(EN.DebertaV3Encoder, cfg, _deb_ref, 100, 700, "C3 2 layers")
+
+
+def test_mt5_c4_stack_two_layers():
+    cfg = dataclasses.replace(EN.MT5Config(), layers=2, vocab=4000)
+    _compare(EN.MT5Encoder, cfg, _t5_ref, 300, 768, "C4 2 layers")
