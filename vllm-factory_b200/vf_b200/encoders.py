@@ -63,9 +63,9 @@ def _layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float) -
 
 
 def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    # T5LayerNorm: no mean subtraction, no bias, variance in fp32 (models/mt5/mt5_encoder.py)
-    var = x.float().pow(2).mean(-1, keepdim=True)
-    return (x.float() * torch.rsqrt(var + eps)).to(x.dtype) * w
+    # T5LayerNorm (no mean subtraction, no bias) as torch's fused RMS norm, which keeps the
+    # variance in fp32 for 16-bit inputs like models/mt5/mt5_encoder.py does
+    return F.rms_norm(x, (x.shape[-1],), w, eps)
 
 
 class DebertaV3Encoder:
