@@ -1,0 +1,35 @@
+"""The torch.ops layer on the CPU: every op has a Meta implementation (shape and dtype of
+the output, for tracing) and raises on CPU tensors (there is no CPU implementation)."""
+import pytest
+import torch
+
+import vf_b200.ops  # noqa: F401
+
+OPS = torch.ops.vf_b200
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_meta_shapes_and_dtypes(dtype):
+    m = dict(device="meta", dtype=dtype)
+    q = torch.empty(2, 3, 100, 64, **m)
+    assert OPS.rpb_attention(q, q, q, None, 32, 128, False, None, 0.0, 1.0).shape == q.shape
+    o = OPS.deberta_attention(q, q, q, None, None, None, False, None, 256, 512, True)
+    assert o.shape == q.shape and o.dtype == dtype
+    qp = torch.empty(100, 3, 64, **m)
+    cu = torch.empty(3, dtype=torch.int32, device="meta")
+    o = OPS.rpb_attention_varlen(qp, qp, qp, cu, 60, None, 32, 128, False, 1.0)
+    assert o.shape == qp.shape and o.dtype == dtype
+    o = OPS.deberta_attention_varlen(qp, qp, qp, cu, 60, None, None, False, None, 256, 512, True)
+    assert o.shape == qp.shape and o.dtype == dtype
+
+
+def test_cpu_tensors_raise():
+    q = torch.zeros(1, 1, 8, 64, dtype=torch.bfloat16)
+    qp = torch.zeros(8, 1, 64, dtype=torch.bfloat16)
+    cu = torch.tensor([0, 8], dtype=torch.int32)
+    for call in (lambda: OPS.rpb_attention(q, q, q, None, 32, 128, False, None, 0.0, 1.0),
+                 lambda: OPS.deberta_attention(q, q, q, None, None, None, False, None, 256, 512, True),
+                 lambda: OPS.rpb_attention_varlen(qp, qp, qp, cu, 8, None, 32, 128, False, 1.0),
+                 lambda: OPS.deberta_attention_varlen(qp, qp, qp, cu, 8, None, None, False, None, 256, 512, True)):
+        with pytest.raises(RuntimeError, match="CUDA"):
+            call()
