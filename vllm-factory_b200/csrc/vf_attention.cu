@@ -51,7 +51,6 @@ constexpr int kBM = 128;          // query rows per tile
 constexpr int kNQ = 2;            // query tiles per work unit (softmax groups per CTA)
 constexpr int kBN = 128;          // keys per tile
 constexpr int kHeadDim = 64;
-constexpr int kStages = 3;        // K/V ring depth
 constexpr int kTileBytes = kBM * kHeadDim * 2;   // 16 KB for a 128 x 64 16-bit tile
 constexpr int kSoftmaxWarps = 4 * kNQ;
 constexpr int kSoftmaxThreads = 32 * kSoftmaxWarps;
@@ -117,45 +116,58 @@ struct __align__(64) KParams {
   short lut[kMaxLut];    // T5: bucket of r = n - m;  DeBERTa: idx of r = m - n
 };
 
-// Shared-memory carve-up (offsets from a 1024-aligned base).  Q is double-buffered by
-// unit, K/V by key tile, the T5 bias table by unit; each group stages its O tile for
-// the bulk store.
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + 2 * kNQ * kTileBytes;
-constexpr int kOffV = kOffK + kStages * kTileBytes;
-constexpr int kOffOStage = kOffV + kStages * kTileBytes;
 constexpr int kRPad = 160;                  // bias-table padding: a warp's window never clamps
 constexpr int kRBiasLen = (kMaxLut + 2 * kRPad + 3) & ~3;
-
-constexpr int kOffKBias = kOffOStage + kNQ * kTileBytes;
-constexpr int kOffKZero = kOffKBias + kStages * kBN * 4;         // per stage: key mask all zero
-constexpr int kOffZeroRow = kOffKZero + 16;                      // kBN zero floats
-constexpr int kOffLut = kOffZeroRow + kBN * 4;
-constexpr int kOffBar = (kOffLut + kMaxLut * 2 + 15) & ~15;
-// barriers: q_full[2], q_empty[2], s_full[2], p_full[2], s_consumed[2], pv_done[2],
-// info_full[2], info_empty[2], stage_free[2], stage_full[2], k_full/v_full/kv_empty[kStages],
-// drain
-constexpr int kNumBars = 20 + 3 * kStages + 1;
-constexpr int kOffMisc = kOffBar + kNumBars * 8;
-constexpr int kOffInfo = kOffMisc + 16;
 constexpr int kMaxLptPairs = 1024;          // (batch, query block) pairs ordered by cost
 constexpr int kMaxLptSamples = 2048;        // T5 mask samples (batch x key tile) for the costs
-constexpr int kOffOrder = kOffInfo + 2 * 64;                      // uint16_t[kMaxLptPairs]
-constexpr int kOffCost = kOffOrder + 2 * kMaxLptPairs;            // uint8_t[kMaxLptPairs]
-// T5-only tables last: the DeBERTa kernel requests shared memory up to kOffLive only, which
-// leaves the SM more L1 cache for its position-term gathers.
-constexpr int kOffLive = kOffCost + kMaxLptPairs;                 // uint8_t[kMaxLptSamples]
-constexpr int kOffRBias = (kOffLive + kMaxLptSamples + 15) & ~15;  // float[2][kRBiasLen]
-constexpr int kSmemBytes = kOffRBias + 2 * kRBiasLen * 4;
-constexpr int kSmemAlloc = kSmemBytes + 1024;
-constexpr int kSmemAllocDeberta = kOffLive + 1024;
-template <int kVariant> constexpr int smem_alloc() { return kVariant == kT5 ? kSmemAlloc : kSmemAllocDeberta; }
+
+// Pipeline depths and shared-memory carve-up (offsets from a 1024-aligned base) per variant.
+// T5: Q double-buffered by unit, a 3-stage K/V ring across units, the bias table by unit.
+// DeBERTa: one Q buffer and a 2-stage ring.  Its time goes to the position-term gathers,
+// which are served by the L1 cache that shares the SM's 256 KB with shared memory: this
+// carve-up (~139 KB with the static part) leaves ~92 KB of L1 where the T5 depths
+// (~203 KB) left ~28 KB.  Each group stages its O tile for the bulk store.
+template <int kVariant>
+struct Smem {
+  static constexpr int kQBuf = kVariant == kDeberta ? 1 : 2;   // Q buffers (units)
+  static constexpr int kKV = kVariant == kDeberta ? 2 : 3;     // K/V ring stages (>= 2)
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + kQBuf * kNQ * kTileBytes;
+  static constexpr int kOffV = kOffK + kKV * kTileBytes;
+  static constexpr int kOffOStage = kOffV + kKV * kTileBytes;
+  static constexpr int kOffKBias = kOffOStage + kNQ * kTileBytes;
+  static constexpr int kOffKZero = kOffKBias + kKV * kBN * 4;    // per stage: key mask all zero
+  static constexpr int kOffZeroRow = kOffKZero + 16;             // kBN zero floats
+  static constexpr int kOffLut = kOffZeroRow + kBN * 4;
+  static constexpr int kOffBar = (kOffLut + kMaxLut * 2 + 15) & ~15;
+  // barriers: q_full[2], q_empty[2], s_full[2], p_full[2], s_consumed[2], pv_done[2],
+  // info_full[2], info_empty[2], stage_free[2], stage_full[2], k_full/v_full/kv_empty[kKV],
+  // drain
+  static constexpr int kNumBars = 20 + 3 * kKV + 1;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kOffInfo = kOffMisc + 16;
+  static constexpr int kOffOrder = kOffInfo + 2 * 64;              // uint16_t[kMaxLptPairs]
+  static constexpr int kOffCost = kOffOrder + 2 * kMaxLptPairs;    // uint8_t[kMaxLptPairs]
+  // T5-only tables last: the DeBERTa kernel requests shared memory up to kOffLive only.
+  static constexpr int kOffLive = kOffCost + kMaxLptPairs;                 // uint8_t[kMaxLptSamples]
+  static constexpr int kOffRBias = (kOffLive + kMaxLptSamples + 15) & ~15;  // float[2][kRBiasLen]
+  static constexpr int kBytes = kVariant == kDeberta ? kOffLive : kOffRBias + 2 * kRBiasLen * 4;
+  static constexpr int kAlloc = kBytes + 1024;
+};
+template <int kVariant> constexpr int smem_alloc() { return Smem<kVariant>::kAlloc; }
+
+// Slot and phase parity of use i of an N-deep ring of buffers and barriers.
+template <int N> __device__ __forceinline__ int ring_slot(int i) { return N == 1 ? 0 : (N == 2 ? (i & 1) : i % N); }
+template <int N> __device__ __forceinline__ uint32_t ring_parity(int i) {
+  return N == 1 ? (i & 1) : (N == 2 ? ((i >> 1) & 1) : (i / N) & 1);
+}
 
 struct SmemMisc {
   uint32_t tmem_base;
   int abort_flag;
 };
-static_assert(kSmemAlloc <= 227 * 1024, "shared memory over the per-CTA limit");
+static_assert(Smem<kT5>::kAlloc <= 227 * 1024 && Smem<kDeberta>::kAlloc <= 227 * 1024,
+              "shared memory over the per-CTA limit");
 
 // One zero position value: the gather of a missing DeBERTa position term reads it with
 // stride 0 (read-only; never written).
@@ -362,14 +374,16 @@ __device__ __forceinline__ bool unit_coords(const KParams& p, const uint16_t* or
 
 template <int kVariant, typename T>
 __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ KParams p) {
+  using S = Smem<kVariant>;
+  constexpr int KV = S::kKV, QB = S::kQBuf;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* kbias = reinterpret_cast<float*>(smem + kOffKBias);
-  float* rbias_buf = reinterpret_cast<float*>(smem + kOffRBias);   // [2][kRBiasLen], index r + R + kRPad
-  int* kzero = reinterpret_cast<int*>(smem + kOffKZero);
-  float* zero_row = reinterpret_cast<float*>(smem + kOffZeroRow);
-  short* lut_s = reinterpret_cast<short*>(smem + kOffLut);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  float* kbias = reinterpret_cast<float*>(smem + S::kOffKBias);
+  float* rbias_buf = reinterpret_cast<float*>(smem + S::kOffRBias);   // [2][kRBiasLen], index r + R + kRPad
+  int* kzero = reinterpret_cast<int*>(smem + S::kOffKZero);
+  float* zero_row = reinterpret_cast<float*>(smem + S::kOffZeroRow);
+  short* lut_s = reinterpret_cast<short*>(smem + S::kOffLut);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kOffBar);
   uint64_t* q_full = bars + 0;        // [2] Q tiles of a unit are in shared memory
   uint64_t* q_empty = bars + 2;       // [2] every QK reading that Q buffer has completed
   uint64_t* s_full = bars + 4;        // [2] S = Q K^T of the tile is in TMEM
@@ -380,13 +394,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   uint64_t* info_empty = bars + 14;   // [2] every role is done with that unit slot
   uint64_t* stage_free = bars + 16;   // [2] the group's previous O store has read its staging tile
   uint64_t* stage_full = bars + 18;   // [2] the group's O rows are staged for the store
-  uint64_t* k_full = bars + 20;       // [kStages]
-  uint64_t* v_full = k_full + kStages;
-  uint64_t* kv_empty = v_full + kStages;
-  uint64_t* drain = kv_empty + kStages;
-  SmemMisc* misc = reinterpret_cast<SmemMisc*>(smem + kOffMisc);
-  UnitInfo* info = reinterpret_cast<UnitInfo*>(smem + kOffInfo);   // [2]
-  int* info_row0 = reinterpret_cast<int*>(smem + kOffInfo + kOffInfoRow0);   // [2]
+  uint64_t* k_full = bars + 20;       // [KV]
+  uint64_t* v_full = k_full + KV;
+  uint64_t* kv_empty = v_full + KV;
+  uint64_t* drain = kv_empty + KV;
+  SmemMisc* misc = reinterpret_cast<SmemMisc*>(smem + S::kOffMisc);
+  UnitInfo* info = reinterpret_cast<UnitInfo*>(smem + S::kOffInfo);   // [2]
+  int* info_row0 = reinterpret_cast<int*>(smem + S::kOffInfo + kOffInfoRow0);   // [2]
   volatile int* abort_flag = &misc->abort_flag;
 
   const int tid = threadIdx.x;
@@ -410,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       mbar_init(&s_consumed[g], kBM);
       mbar_init(&pv_done[g], 1);
     }
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < KV; ++s) {
       mbar_init(&k_full[s], has_mask ? 2 : 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], kMmaIssuers);
@@ -434,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
   if (tid < kBN) zero_row[tid] = 0.f;
   // T5 mask samples for the unit costs (one load per thread for typical sizes).
   if (has_mask && lpt_enabled<kVariant>(p)) {
-    uint8_t* live = smem + kOffLive;
+    uint8_t* live = smem + S::kOffLive;
     const int ntile = (p.N + kBN - 1) / kBN;
     for (int it = tid; it < p.B * ntile; it += kThreads) {
       const int b = it / ntile, kt = it % ntile;
@@ -452,14 +466,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     // ------------------------------------------------------------ unit preparation
     // Describes unit i in slot i & 1: live key range (mask scan), and for T5 the bias
     // table of the unit's head.  Runs one unit ahead of the other roles.
-    uint16_t* order = reinterpret_cast<uint16_t*>(smem + kOffOrder);
-    uint8_t* cost = smem + kOffCost;
+    uint16_t* order = reinterpret_cast<uint16_t*>(smem + S::kOffOrder);
+    uint8_t* cost = smem + S::kOffCost;
     const int nqb = (p.M + kNQ * kBM - 1) / (kNQ * kBM);
     const bool lpt = lpt_enabled<kVariant>(p);
     if (lpt) {
       // Stable counting sort of the pairs by estimated cost, descending.
       const int P = p.B * nqb;
-      const uint8_t* live = smem + kOffLive;
+      const uint8_t* live = smem + S::kOffLive;
       int maxc = 0;
       for (int pi = lane; pi < P; pi += 32) {
         const int c = min(pair_cost<kVariant>(p, live, pi / nqb, pi % nqb), 255);
@@ -564,21 +578,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       if (lane == 0) mbar_arrive(&info_empty[slot]);
       if (!u.valid) break;
       if (u.nkv == 0) continue;
-      const int qs = qi & 1;
-      if (qi >= 2) {
-        const bool ok = mbar_wait(&q_empty[qs], ((qi - 2) >> 1) & 1, abort_flag);
+      const int qs = ring_slot<QB>(qi);
+      if (qi >= QB) {
+        const bool ok = mbar_wait(&q_empty[qs], ring_parity<QB>(qi - QB), abort_flag);
         if (!__all_sync(0xffffffffu, ok)) break;
       }
       if (lane == 0) {
         mbar_arrive_expect_tx(&q_full[qs], kNQ * kTileBytes);
         for (int g = 0; g < kNQ; ++g)
-          tma_load_4d(smem + kOffQ + (qs * kNQ + g) * kTileBytes, &p.tm_q, &q_full[qs], 0, row0 + u.q0 + g * kBM, u.h, bc);
+          tma_load_4d(smem + S::kOffQ + (qs * kNQ + g) * kTileBytes, &p.tm_q, &q_full[qs], 0, row0 + u.q0 + g * kBM, u.h, bc);
       }
       ++qi;
       bool stop = false;
       for (int t = 0; t < u.nkv; ++t, ++gt) {
-        const int s = gt % kStages;
-        const int round = gt / kStages;
+        const int s = gt % KV;
+        const int round = gt / KV;
         if (round > 0) {
           const bool ok = mbar_wait(&kv_empty[s], (round - 1) & 1, abort_flag);
           if (!__all_sync(0xffffffffu, ok)) { stop = true; break; }
@@ -586,9 +600,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         const int k0 = (u.t_begin + t) * kBN;
         if (lane == 0) {
           mbar_arrive_expect_tx(&k_full[s], kTileBytes);
-          tma_load_4d(smem + kOffK + s * kTileBytes, &p.tm_k, &k_full[s], 0, row0 + k0, u.h, bc);
+          tma_load_4d(smem + S::kOffK + s * kTileBytes, &p.tm_k, &k_full[s], 0, row0 + k0, u.h, bc);
           mbar_arrive_expect_tx(&v_full[s], kTileBytes);
-          tma_load_4d(smem + kOffV + s * kTileBytes, &p.tm_v, &v_full[s], 0, row0 + k0, u.h, bc);
+          tma_load_4d(smem + S::kOffV + s * kTileBytes, &p.tm_v, &v_full[s], 0, row0 + k0, u.h, bc);
         }
         if (has_mask) {
           bool zero = true;
@@ -613,10 +627,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
     // No TMA write may land after this CTA exits: wait for the last fills (already
     // complete on the normal path), ignoring the abort flag but still time-bounded.
     if (lane == 0) {
-      for (int j = max(qi - 2, 0); j < qi; ++j) mbar_wait_bounded(&q_full[j & 1], (j >> 1) & 1);
-      for (int t = max(gt - kStages, 0); t < gt; ++t) {
-        mbar_wait_bounded(&k_full[t % kStages], (t / kStages) & 1);
-        mbar_wait_bounded(&v_full[t % kStages], (t / kStages) & 1);
+      for (int j = max(qi - QB, 0); j < qi; ++j) mbar_wait_bounded(&q_full[ring_slot<QB>(j)], ring_parity<QB>(j));
+      for (int t = max(gt - KV, 0); t < gt; ++t) {
+        mbar_wait_bounded(&k_full[t % KV], (t / KV) & 1);
+        mbar_wait_bounded(&v_full[t % KV], (t / KV) & 1);
       }
     }
   } else if (warp == kMmaWarp || (kMmaIssuers == 2 && warp == kMmaWarp2)) {
@@ -628,9 +642,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       constexpr uint32_t fmt = AbFormat<T>::value;
       constexpr uint32_t idesc_qk = idesc_f16(fmt, kBM, kBN, 0, 0);
       constexpr uint32_t idesc_pv = idesc_f16(fmt, kBM, kHeadDim, 0, 1);
-      const uint32_t sQ = smem_u32(smem + kOffQ);
-      const uint32_t sK = smem_u32(smem + kOffK);
-      const uint32_t sV = smem_u32(smem + kOffV);
+      const uint32_t sQ = smem_u32(smem + S::kOffQ);
+      const uint32_t sK = smem_u32(smem + S::kOffK);
+      const uint32_t sV = smem_u32(smem + S::kOffV);
       auto issue_qk = [&](int g, int qs, int s) {
 #pragma unroll
         for (int kk = 0; kk < kHeadDim / 16; ++kk) {
@@ -667,15 +681,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       int G = 0;           // global tile index of the cursor
       // First tile of a unit: S = Q K^T for both groups (the S columns are free).
       auto start_unit = [&]() -> bool {
-        if (!mbar_wait(&q_full[qi & 1], (qi >> 1) & 1, abort_flag) ||
-            !mbar_wait(&k_full[G % kStages], (G / kStages) & 1, abort_flag))
+        if (!mbar_wait(&q_full[ring_slot<QB>(qi)], ring_parity<QB>(qi), abort_flag) ||
+            !mbar_wait(&k_full[G % KV], (G / KV) & 1, abort_flag))
           return false;
         tc_fence_after();
         for (int g = g_lo; g < g_hi; ++g) {
-          issue_qk(g, qi & 1, G % kStages);
+          issue_qk(g, ring_slot<QB>(qi), G % KV);
           umma_commit(&s_full[g]);
         }
-        if (cur_nkv == 1) umma_commit(&q_empty[qi & 1]);
+        if (cur_nkv == 1) umma_commit(&q_empty[ring_slot<QB>(qi)]);
         return true;
       };
       bool have = next_unit(cur_nkv);
@@ -689,21 +703,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       // a unit overwrites O: the softmax threads have read the previous unit's O before
       // they publish that P.
       while (have && ok) {
-        const int s = G % kStages;
+        const int s = G % KV;
         const bool more = cur_t + 1 < cur_nkv;
-        const int s2 = (G + 1) % kStages;
-        if (more && !mbar_wait(&k_full[s2], ((G + 1) / kStages) & 1, abort_flag)) break;
+        const int s2 = (G + 1) % KV;
+        if (more && !mbar_wait(&k_full[s2], ((G + 1) / KV) & 1, abort_flag)) break;
         for (int g = g_lo; g < g_hi && ok; ++g) {
           if (!mbar_wait(&s_consumed[g], G & 1, abort_flag)) { ok = false; break; }
           if (more) {
             tc_fence_after();
-            issue_qk(g, qi & 1, s2);
+            issue_qk(g, ring_slot<QB>(qi), s2);
             umma_commit(&s_full[g]);
           }
         }
         if (!ok) break;
-        if (more && cur_t + 2 == cur_nkv) umma_commit(&q_empty[qi & 1]);
-        if (!mbar_wait(&v_full[s], (G / kStages) & 1, abort_flag)) break;
+        if (more && cur_t + 2 == cur_nkv) umma_commit(&q_empty[ring_slot<QB>(qi)]);
+        if (!mbar_wait(&v_full[s], (G / KV) & 1, abort_flag)) break;
         for (int g = g_lo; g < g_hi && ok; ++g) {
           if (!mbar_wait(&p_full[g], G & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
@@ -769,10 +783,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
       float l_run = 0.f;
       int k0 = vu->t_begin * kBN;
       for (int t = 0; t < nkv; ++t, ++G, k0 += kBN) {
-        const int st = G % kStages;
+        const int st = G % KV;
         const float* rbias = rbias_buf + slot * kRBiasLen;
         bool ok = mbar_wait(&s_full[g], G & 1, abort_flag);
-        if (has_mask) ok = ok && mbar_wait(&k_full[st], (G / kStages) & 1, abort_flag);
+        if (has_mask) ok = ok && mbar_wait(&k_full[st], (G / KV) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
         tc_fence_after();
         // Scores in log2 units.  TMEM is read 32 columns at a time (bounded register
@@ -824,7 +838,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         } else {
           // Position rows are rows row0 + m / row0 + n of the views (row0 = 0 unless the batch
           // is packed, whose single-batch views have their batch strides set to 0 by the host).
-          const int row0 = reinterpret_cast<const volatile int*>(smem + kOffInfo + kOffInfoRow0)[slot];
+          const int row0 = reinterpret_cast<const volatile int*>(smem + S::kOffInfo + kOffInfoRow0)[slot];
           const int b = vu->b, h = vu->h, klen = vu->klen;
           // Position terms.  A missing term (or a row past the sequence, whose output is zero
           // or not written) reads one zero element with stride 0, so the gather loop has no
@@ -962,7 +976,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         const bool use = have && mine && l_run > 0.f;
         const float inv_l = use ? 1.f / l_run : 0.f;
         bulk_wait_read_all();                // this thread's previous row copy has read its row
-        uint8_t* srow = smem + kOffOStage + g * kTileBytes + row * 128;
+        uint8_t* srow = smem + S::kOffOStage + g * kTileBytes + row * 128;
 #pragma unroll
         for (int ch = 0; ch < kHeadDim / 16; ++ch) {
           uint32_t o[16];
@@ -988,7 +1002,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         if (mine) {
           fence_proxy_async_smem();
           T* dst = reinterpret_cast<T*>(p.out) + vu->h * p.o_sh +
-                   (long long)(reinterpret_cast<const volatile int*>(smem + kOffInfo + kOffInfoRow0)[slot] + m) * p.o_sm;
+                   (long long)(reinterpret_cast<const volatile int*>(smem + S::kOffInfo + kOffInfoRow0)[slot] + m) * p.o_sm;
           bulk_copy_s2g(dst, srow, kHeadDim * 2);
           bulk_commit();
         }
@@ -1005,7 +1019,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           mbar_arrive(&stage_free[g]);
         }
         const bool okf = mbar_wait(&stage_free[g], i & 1, abort_flag);
-        uint8_t* stg = smem + kOffOStage + g * kTileBytes + row * 128;
+        uint8_t* stg = smem + S::kOffOStage + g * kTileBytes + row * 128;
         if (okf) {
           // O is read 16 columns at a time (`have` is warp-uniform: the load is collective).
 #pragma unroll
@@ -1034,7 +1048,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         }
         mbar_arrive(&stage_full[g]);
         if (row == 0 && mbar_wait(&stage_full[g], i & 1, abort_flag)) {
-          tma_store_4d(&p.tm_o, smem + kOffOStage + g * kTileBytes, 0, vu->q0 + g * kBM, vu->h, vu->b);
+          tma_store_4d(&p.tm_o, smem + S::kOffOStage + g * kTileBytes, 0, vu->q0 + g * kBM, vu->h, vu->b);
           bulk_commit();
         }
         if (!__all_sync(0xffffffffu, okf)) aborted = true;
