@@ -281,7 +281,8 @@ def encoder_cpu_baseline(name: str, budget_s: float = 15.0):
     else:
         fn = lambda q, k, v, cu, ms, t, nb, md, dec, sc: oracle.rpb_attention_varlen_ref(
             q, k, v, cu, t, nb, md, dec, sc, dtype=torch.float32)
-    model = cls(small, device="cpu", dtype=torch.float32, seed=0, attention_fn=fn)
+    extra = {} if name == "deberta_c3" else {"gated_act": lambda g, u, a: oracle.gated_act_ref(g, u, 0)}
+    model = cls(small, device="cpu", dtype=torch.float32, seed=0, attention_fn=fn, **extra)
     done, n, t0 = 0, 0, time.perf_counter()
     while time.perf_counter() - t0 < budget_s and n < len(lengths):
         x, cu, lens = EN.select_sequences(lengths, ids, [n])
@@ -381,6 +382,84 @@ def run_encoder(args, world: int, rank: int, dev, warmup: int):
     return line
 
 
+# ----------------------------------------------------------------------------- FFN activation
+def gated_act_cpu_baseline(budget_s: float = 10.0):
+    """The oracle of the reference's kernel arithmetic (fp32 torch) on the host cores over
+    a 2048-row slice of the workload, repeated for ~10 s: GB/s of the same bytes."""
+    import oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(4000)
+    gu = (torch.randn(2048, 2 * 2816, generator=g) * 2).to(torch.bfloat16)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        oracle.gated_act_ref(gu[:, :2816], gu[:, 2816:], 0)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n * 3 * 2048 * 2816 * 2 / dt / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{n} x 2048 rows of the 16384 x 2816 workload, fp32 torch on CPU (oracle)"}
+
+
+def run_gated_act(args, world: int, rank: int, dev, warmup: int):
+    """mt5_ffn_act: the gated-GELU of one mT5-large FFN (kernels.ff_fused drop-in) on the
+    two halves of a stacked [16384, 2 x 2816] bf16 projection, read in place.  HBM-bound:
+    value = bytes moved (gate + up read, out written) / time, in GB/s."""
+    from kernels.ff_fused import fused_gelu_mul_dropout
+    T, Fd = 16384, 2816
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    sets = [(torch.randn(T, 2 * Fd, generator=g, device=dev) * 2).to(torch.bfloat16) for _ in range(3)]
+    nbytes = 3 * T * Fd * 2
+    stream = torch.cuda.current_stream(dev)
+    call = lambda gu: fused_gelu_mul_dropout(gu[:, :Fd], gu[:, Fd:], "gelu_new")
+    for i in range(warmup):
+        call(sets[i % 3])
+    torch.cuda.synchronize()
+    sampler = ClockSampler(dev.index or 0)
+    sampler.start()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        call(sets[i % 3])
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1)
+    from vf_b200 import dist as VD
+    ms_max, bytes_all, _ = VD.reduce_timing(ms, float(nbytes), 0.0, dev)
+    value = bytes_all * args.steps / (ms_max * 1e-3) / 1e9
+    e2e = None
+    if not args.no_e2e:
+        host = sets[0].cpu().pin_memory()
+        out_host = torch.empty(T, Fd, dtype=torch.bfloat16).pin_memory()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_e2e = max(3, min(args.steps, 10))
+        e0.record(stream)
+        for _ in range(n_e2e):
+            out_host.copy_(call(host.to(dev, non_blocking=True)), non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ems, _, _ = VD.reduce_timing(e0.elapsed_time(e1), 0.0, 0.0, dev)
+        e2e = {"value": bytes_all * n_e2e / (ems * 1e-3) / 1e9, "unit": "GB/s",
+               "h2d_bytes_per_step": int(host.numel() * 2), "d2h_bytes_per_step": int(out_host.numel() * 2),
+               "steps": n_e2e}
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    achieved = nbytes / (ms / args.steps * 1e-3) / 1e9
+    return {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "mT5-large FFN gated-GELU (kernels/ff_fused.py drop-in), 16384 x 2816, halves of a stacked projection",
+                       "l2": "3 rotating 185 MB input sets > L2; no flush"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks.get("hbm", 6650.0), "unit": "GB/s",
+                         "frac": achieved / peaks.get("hbm", 6650.0), "traffic": committed_traffic(args.workload),
+                         "peak_source": f"{peaks['source']} HBM copy", "algorithmic_bytes_per_launch": nbytes},
+            "gpu_launches": args.steps, "clocks": clocks, "e2e": e2e,
+            **({"cpu_baseline": gated_act_cpu_baseline()} if world == 1 and not args.no_cpu_baseline else {})}
+
+
 # ----------------------------------------------------------------------------- main
 def main():
     ap = argparse.ArgumentParser()
@@ -403,6 +482,8 @@ def main():
             return
         if args.workload in ENCODER_WORKLOADS:
             cb = encoder_cpu_baseline(args.workload)
+        elif args.workload == "mt5_ffn_act":
+            cb = gated_act_cpu_baseline()
         else:
             cb = cpu_baseline(args.workload, None, budget_s=max(5.0, min(60.0, 2.0 * args.steps)))
         line = {"metric": METRIC, "value": cb["value"], "unit": cb["unit"], "n_gpus": args.gpus, "steps": args.steps,
@@ -426,8 +507,9 @@ def main():
     import vf_b200
     vf_b200.load()
 
-    if args.workload in ENCODER_WORKLOADS:
-        line = run_encoder(args, world, rank, dev, warmup)
+    if args.workload in ENCODER_WORKLOADS or args.workload == "mt5_ffn_act":
+        runner = run_gated_act if args.workload == "mt5_ffn_act" else run_encoder
+        line = runner(args, world, rank, dev, warmup)
         if line is not None:
             print(json.dumps(line))
         if world > 1:

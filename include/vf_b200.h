@@ -138,6 +138,30 @@ int vf_deberta_attention_varlen_fwd(const vf_deberta_attention_args_t* args, con
                                     int32_t num_seqs, int32_t max_seqlen, void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * Gated activation of the mT5 feed-forward: out = act(gate) * up, in fp32, rounded to the
+ * dtype.  Replaces kernels/ff_fused.py:86 `fused_gelu_mul_dropout(gate, up, act_fn,
+ * dropout_p, training)` and its kernel (:23-74) on the inference path (no dropout).
+ * gate, up, out: rows x cols views of one dtype (f32/f16/bf16) with unit column stride and
+ * the given row strides in elements (>= cols); e.g. the two halves of a stacked [T, 2F]
+ * projection.  act: VF_ACT_GELU_TANH for 'gelu' / 'gelu_new' / 'gelu_fast' /
+ * 'gelu_pytorch_tanh', VF_ACT_GELU_ERF for 'gelu_accurate', VF_ACT_RELU, VF_ACT_SILU
+ * ('silu' / 'swish') -- the reference's _act_type_map (:77-85).
+ * ------------------------------------------------------------------------------------ */
+enum { VF_ACT_GELU_TANH = 0, VF_ACT_GELU_ERF = 1, VF_ACT_RELU = 2, VF_ACT_SILU = 3 };
+
+typedef struct {
+  vf_dtype_t dtype;
+  const void* gate;
+  const void* up;
+  void* out;
+  int64_t rows, cols;
+  int64_t gate_row_stride, up_row_stride, out_row_stride;
+  int32_t act;
+} vf_gated_act_args_t;
+
+int vf_gated_act_fwd(const vf_gated_act_args_t* args, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Host-side bucket functions (no GPU needed).  These are the exact integer outputs the
  * kernels use; they restate, in float32 arithmetic like the reference's torch code:
  *  - models/mt5/mt5_encoder.py:125 T5RelativePositionBias._relative_position_bucket

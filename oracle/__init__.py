@@ -17,6 +17,7 @@ It restates, in plain PyTorch on the CPU, the reference's own algorithms for the
                       :295-299, :334); the packed form applies it to each cu_seqlens
                       sequence alone
   * DeBERTa layer:    models/deberta_v2/deberta_v2_encoder.py:332-487 (_pytorch_forward)
+  * mT5 FFN act:      kernels/ff_fused.py:23-74 (fused_gelu_mul_dropout's kernel, no dropout)
 
 Parity pinning: tests/golden/make_golden.py runs the reference's own functions (imported
 from the read-only reference checkout in the build container) and commits their outputs
@@ -32,3 +33,4 @@ from .rpb import (  # noqa: F401
     t5_bias_dense_ref,
     t5_relative_bucket_ref,
 )
+from .ffn import gated_act_ref  # noqa: F401,E402

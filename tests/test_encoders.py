@@ -18,6 +18,10 @@ def _t5_attn(q, k, v, cu, ms, t, nb, md, dec, sc):
     return oracle.rpb_attention_varlen_ref(q, k, v, cu, t, nb, md, dec, sc, dtype=torch.float32)
 
 
+def _gated_act(gate, up, act_fn):
+    return oracle.gated_act_ref(gate, up, 0)
+
+
 def _packing_invariance(model, vocab):
     lengths, ids = EN.packed_batch(4, 3, 40, vocab, seed=1)
     x, cu, lens = EN.select_sequences(lengths, ids, range(4))
@@ -38,7 +42,8 @@ def test_deberta_encoder_packing_invariance():
 
 def test_mt5_encoder_packing_invariance():
     cfg = dataclasses.replace(EN.MT5Config(), layers=2, hidden=128, heads=2, ffn=160, vocab=500)
-    _packing_invariance(EN.MT5Encoder(cfg, device="cpu", dtype=torch.float32, attention_fn=_t5_attn), 500)
+    _packing_invariance(EN.MT5Encoder(cfg, device="cpu", dtype=torch.float32, attention_fn=_t5_attn,
+                                       gated_act=_gated_act), 500)
 
 
 def test_deberta_position_scores_are_q_dot_kr():

@@ -21,6 +21,9 @@ def test_meta_shapes_and_dtypes(dtype):
     assert o.shape == qp.shape and o.dtype == dtype
     o = OPS.deberta_attention_varlen(qp, qp, qp, cu, 60, None, None, False, None, 256, 512, True)
     assert o.shape == qp.shape and o.dtype == dtype
+    g = torch.empty(5, 7, 2816, **m)
+    o = OPS.gated_act(g, g, 0)
+    assert o.shape == g.shape and o.dtype == dtype
 
 
 def test_cpu_tensors_raise():
@@ -30,6 +33,7 @@ def test_cpu_tensors_raise():
     for call in (lambda: OPS.rpb_attention(q, q, q, None, 32, 128, False, None, 0.0, 1.0),
                  lambda: OPS.deberta_attention(q, q, q, None, None, None, False, None, 256, 512, True),
                  lambda: OPS.rpb_attention_varlen(qp, qp, qp, cu, 8, None, 32, 128, False, 1.0),
-                 lambda: OPS.deberta_attention_varlen(qp, qp, qp, cu, 8, None, None, False, None, 256, 512, True)):
+                 lambda: OPS.deberta_attention_varlen(qp, qp, qp, cu, 8, None, None, False, None, 256, 512, True),
+                 lambda: OPS.gated_act(q, q, 0)):
         with pytest.raises(RuntimeError, match="CUDA"):
             call()

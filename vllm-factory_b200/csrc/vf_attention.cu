@@ -1394,6 +1394,11 @@ int finish_deberta_table(const vf_deberta_attention_args_t* a, int span_rows, vf
 
 }  // namespace
 
+namespace vf {
+// The thread's last error message, for the other translation units of the library.
+__attribute__((visibility("hidden"))) int set_last_error(int code, const std::string& msg) { return fail(code, msg); }
+}  // namespace vf
+
 extern "C" {
 
 const char* vf_last_error(void) { return g_last_error.c_str(); }

@@ -303,6 +303,57 @@ at::Tensor deberta_attention_varlen(const at::Tensor& q_in, const at::Tensor& k_
   return f32 ? out.to(at::kFloat) : out;
 }
 
+// Gated activation: out = act(gate) * up over the last dimension; leading dimensions are
+// rows.  Each operand only needs a unit stride on the last dimension and leading
+// dimensions that collapse to one row stride (as the two column halves of a 2-D [T, 2F]
+// projection do); anything else is copied contiguous first.
+at::Tensor gated_act(const at::Tensor& gate_in, const at::Tensor& up_in, int64_t act) {
+  require_cuda(gate_in, "gate");
+  require_cuda(up_in, "up");
+  TORCH_CHECK(gate_in.sizes() == up_in.sizes(), "vf_b200: gate and up must have identical shapes");
+  TORCH_CHECK(gate_in.scalar_type() == up_in.scalar_type(), "vf_b200: gate and up must share a dtype");
+  TORCH_CHECK(gate_in.dim() >= 1, "vf_b200: gate must have at least one dimension");
+  c10::cuda::CUDAGuard guard(gate_in.device());
+  const int64_t cols = gate_in.size(-1);
+  const int64_t rows = cols == 0 ? 0 : gate_in.numel() / cols;
+  // A 2-D (rows, cols) view with unit column stride, without a copy when possible.
+  auto as_rows = [&](const at::Tensor& t) {
+    at::Tensor x = t;
+    if (x.dim() == 1) x = x.unsqueeze(0);
+    if (x.stride(-1) != 1) x = x.contiguous();
+    if (x.dim() > 2) {
+      bool collapses = true;   // leading dims form one row stride
+      for (int64_t d = x.dim() - 2; d > 0; --d)
+        if (x.size(d - 1) > 1 && x.stride(d - 1) != x.stride(d) * x.size(d)) collapses = false;
+      if (!collapses) x = x.contiguous();
+      x = x.reshape({rows, cols});
+    }
+    if (x.size(0) > 1 && x.stride(0) < cols) x = x.contiguous();   // overlapping or broadcast rows
+    return x;
+  };
+  const at::Tensor g = as_rows(gate_in), u = as_rows(up_in);
+  at::Tensor out = at::empty(gate_in.sizes(), gate_in.options());
+  if (rows == 0 || cols == 0) return out;
+  vf_gated_act_args_t a{};
+  a.dtype = dtype_code(g);
+  a.gate = g.data_ptr();
+  a.up = u.data_ptr();
+  a.out = out.data_ptr();
+  a.rows = rows;
+  a.cols = cols;
+  a.gate_row_stride = rows > 1 ? g.stride(0) : cols;
+  a.up_row_stride = rows > 1 ? u.stride(0) : cols;
+  a.out_row_stride = cols;
+  a.act = static_cast<int32_t>(act);
+  check_rc(vf_gated_act_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
+  return out;
+}
+
+at::Tensor gated_act_meta(const at::Tensor& gate, const at::Tensor&, int64_t) { return at::empty_like(gate); }
+at::Tensor gated_act_cpu(const at::Tensor&, const at::Tensor&, int64_t) {
+  TORCH_CHECK(false, "vf_b200: gate and up must be CUDA tensors (no CPU implementation)");
+}
+
 // Shape functions for tracing (torch.compile / fake tensors).
 at::Tensor rpb_attention_meta(const at::Tensor& q, const at::Tensor&, const at::Tensor&,
                               const std::optional<at::Tensor>&, int64_t, int64_t, bool,
@@ -358,6 +409,7 @@ TORCH_LIBRARY(vf_b200, m) {
   m.def("deberta_attention(Tensor q, Tensor k, Tensor v, Tensor? seq_lengths, Tensor? pos_key, "
         "Tensor? pos_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "
         "bool use_log_bucket) -> Tensor");
+  m.def("gated_act(Tensor gate, Tensor up, int act) -> Tensor");
   m.def("deberta_attention_varlen(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, int max_seqlen, Tensor? pos_key, "
         "Tensor? pos_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "
         "bool use_log_bucket) -> Tensor");
@@ -368,6 +420,7 @@ TORCH_LIBRARY_IMPL(vf_b200, CUDA, m) {
   m.impl("rpb_attention_varlen", &rpb_attention_varlen);
   m.impl("deberta_attention", &deberta_attention);
   m.impl("deberta_attention_varlen", &deberta_attention_varlen);
+  m.impl("gated_act", &gated_act);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
@@ -375,6 +428,7 @@ TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
   m.impl("rpb_attention_varlen", &rpb_attention_varlen_cpu);
   m.impl("deberta_attention", &deberta_attention_cpu);
   m.impl("deberta_attention_varlen", &deberta_attention_varlen_cpu);
+  m.impl("gated_act", &gated_act_cpu);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
@@ -382,4 +436,5 @@ TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
   m.impl("rpb_attention_varlen", &rpb_attention_varlen_meta);
   m.impl("deberta_attention", &deberta_attention_meta);
   m.impl("deberta_attention_varlen", &deberta_attention_varlen_meta);
+  m.impl("gated_act", &gated_act_meta);
 }

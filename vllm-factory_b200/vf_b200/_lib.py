@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "vf_rpb_attention_varlen_fwd",
     "vf_deberta_attention_fwd",
     "vf_deberta_attention_varlen_fwd",
+    "vf_gated_act_fwd",
     "vf_t5_relative_bucket",
     "vf_deberta_log_bucket",
     "vf_last_error",
@@ -68,6 +69,24 @@ class RpbArgs(ctypes.Structure):
         ("mask_dtype", ctypes.c_int),
         ("dropout_p", ctypes.c_float),
         ("softmax_scale", ctypes.c_float),
+    ]
+
+
+VF_ACT_GELU_TANH, VF_ACT_GELU_ERF, VF_ACT_RELU, VF_ACT_SILU = 0, 1, 2, 3
+
+
+class GatedActArgs(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_int),
+        ("gate", ctypes.c_void_p),
+        ("up", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+        ("gate_row_stride", ctypes.c_int64),
+        ("up_row_stride", ctypes.c_int64),
+        ("out_row_stride", ctypes.c_int64),
+        ("act", ctypes.c_int32),
     ]
 
 
@@ -125,6 +144,8 @@ def load() -> ctypes.CDLL:
         lib.vf_deberta_attention_varlen_fwd.argtypes = [ctypes.POINTER(DebertaArgs), ctypes.c_void_p,
                                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
         lib.vf_deberta_attention_varlen_fwd.restype = ctypes.c_int
+        lib.vf_gated_act_fwd.argtypes = [ctypes.POINTER(GatedActArgs), ctypes.c_void_p]
+        lib.vf_gated_act_fwd.restype = ctypes.c_int
         lib.vf_t5_relative_bucket.argtypes = [ctypes.c_int32] * 5 + [ctypes.POINTER(ctypes.c_int32)]
         lib.vf_t5_relative_bucket.restype = ctypes.c_int
         lib.vf_deberta_log_bucket.argtypes = [ctypes.c_int32] * 4 + [ctypes.POINTER(ctypes.c_int32)]

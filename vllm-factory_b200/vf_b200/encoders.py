@@ -11,7 +11,8 @@ stacks measure encoder tokens/s with the hot path in place:
                     rel_embeddings + LayerNorm, GELU FFN, post-LayerNorm residuals).
   MT5Encoder        models/mt5/mt5_encoder.py (T5 RMS LayerNorm, no QK scaling, the bias
                     table of layer 0 shared by all layers :546-566, gated-GELU FFN with the
-                    tanh GELU, final RMS norm).
+                    tanh GELU through this package's fused_gelu_mul_dropout as at :418,
+                    final RMS norm).
 
 Position scores for DeBERTa are formed per packed row: pos_key[t, h, :] = q[t, h] . Kr[:, h]
 and pos_query[t, h, :] = k[t, h] . Qr[:, h] (Kr = key_proj(rel), Qr = query_proj(rel),
@@ -125,11 +126,12 @@ class DebertaV3Encoder:
 
 
 class MT5Encoder:
-    """mT5 encoder over a packed batch; attention = flash_attention_rpb_varlen (or
-    `attention_fn` of the same signature)."""
+    """mT5 encoder over a packed batch; attention = flash_attention_rpb_varlen and the
+    gated-GELU of the FFN = fused_gelu_mul_dropout (or `attention_fn` / `gated_act` of the
+    same signatures)."""
 
     def __init__(self, cfg: MT5Config = MT5Config(), device="cuda", dtype=torch.bfloat16, seed: int = 0,
-                 attention_fn=None):
+                 attention_fn=None, gated_act=None):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         g = torch.Generator(device=self.device).manual_seed(seed)
         E, F_ = cfg.hidden, cfg.ffn
@@ -146,6 +148,9 @@ class MT5Encoder:
         if attention_fn is None:
             from kernels.flash_attention_rpb import flash_attention_rpb_varlen as attention_fn
         self.attention_fn = attention_fn
+        if gated_act is None:
+            from kernels.ff_fused import fused_gelu_mul_dropout as gated_act
+        self.gated_act = gated_act
 
     @torch.no_grad()
     def forward(self, ids: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
@@ -160,7 +165,7 @@ class MT5Encoder:
             h = h + ctx.reshape(T, E).to(h.dtype) @ L["wo"].t()
             x = _rms_norm(h, L["ln2"], cfg.eps)
             gu = x @ L["wi"].t()
-            f = F.gelu(gu[:, :F_], approximate="tanh") * gu[:, F_:]
+            f = self.gated_act(gu[:, :F_], gu[:, F_:], "gelu_new")     # gated-GELU, halves read in place
             h = h + f @ L["wo_ff"].t()
         return _rms_norm(h, self.final_ln, cfg.eps)
 

@@ -15,6 +15,8 @@ strides and the current CUDA stream and calls the C ABI of libvf_b200.so:
                                              pos_query?, causal, sm_scale?, position_buckets,
                                              max_relative_distance, use_log_bucket)   # packed
 
+  torch.ops.vf_b200.gated_act(gate, up, act)                  # mT5 FFN: act(gate) * up
+
 All borrow their inputs (layouts TMA cannot describe are copied contiguous), allocate
 only the output, launch on the caller's stream, and have Meta implementations for
 tracing.  CPU tensors raise: there is no CPU implementation.
@@ -39,3 +41,4 @@ rpb_attention = torch.ops.vf_b200.rpb_attention
 rpb_attention_varlen = torch.ops.vf_b200.rpb_attention_varlen
 deberta_attention = torch.ops.vf_b200.deberta_attention
 deberta_attention_varlen = torch.ops.vf_b200.deberta_attention_varlen
+gated_act = torch.ops.vf_b200.gated_act
