@@ -859,20 +859,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           tmem_ld_2x64_f2(tS, x2);
           tc_fence_before();
           mbar_arrive(&s_consumed[g]);
-          // Warp-uniform: where the index is r + const over the warp's whole window
-          // (DeBERTa's exact bucket range), it is computed instead of looked up.
-          const int m0 = m - lane;
-          const int r_lo = m0 - (k0 + kBN - 1), r_hi = m0 + 31 - k0;
-          bool linear = r_lo >= -R && r_hi <= R;
-          int off = 0;
-          if (linear) {
-            off = lut_s[r_lo + R] - r_lo;
-            linear = (lut_s[r_hi + R] - r_hi) == off;
-          }
+          // Every index comes from the shared-memory LUT.  (A warp-uniform arithmetic path
+          // for windows inside the exact bucket range, idx = r + const, was 11-13 % slower:
+          // the select kept both paths in the unrolled loop.)
 #pragma unroll
           for (int c = 0; c < kBN; ++c) {
             const int n = min(k0 + c, klen - 1);   // keys past klen are masked below
-            const int idx = linear ? m - n + off : lut_s[min(max(m - n, -R), R) + R];
+            const int idx = lut_s[min(max(m - n, -R), R) + R];
             const float add = to_f<T>(pk_row[idx * pk_sk]) + to_f<T>(pq_bh[(long long)n * pq_sn + idx * pq_sk]);
             if (c & 1) x2[c >> 1].y = (x2[c >> 1].y + add) * scale_log2;
             else x2[c >> 1].x = (x2[c >> 1].x + add) * scale_log2;
