@@ -156,3 +156,22 @@ def test_deberta_varlen_validation_rejects_before_launch():
     assert lib.vf_deberta_attention_varlen_fwd(ctypes.byref(a), None, 2, 100, None) == _lib.VF_EINVAL
     assert lib.vf_deberta_attention_varlen_fwd(ctypes.byref(a), 0x20000, 2, 301, None) == _lib.VF_EINVAL
     assert "max_seqlen" in lib.vf_last_error().decode()
+
+
+def test_deberta_position_strides_beyond_32_bit_offsets_rejected():
+    """The gathers use 32-bit offsets inside a key tile; views whose strides could overflow
+    them are refused before any launch."""
+    lib = _lib.load()
+    a = _lib.DebertaArgs()
+    a.dtype = _lib.VF_DTYPE_BF16
+    shape = (2, 4, 256, 64)
+    a.q, a.k, a.v, a.out = (_fake_t4(shape, 0x10000 * (i + 1)) for i in range(4))
+    a.position_buckets, a.max_relative_distance, a.use_log_bucket = 256, 512, 1
+    a.pos_query = _fake_t4((2, 4, 256, 512), 0x90000)
+    a.pos_query.stride[2] = 1 << 25            # 127 * 2^25 > 2^31
+    assert lib.vf_deberta_attention_fwd(ctypes.byref(a), None) == _lib.VF_EUNSUPPORTED
+    assert "32-bit" in lib.vf_last_error().decode()
+    a.pos_query = _lib.Tensor4d()
+    a.pos_key = _fake_t4((2, 4, 256, 512), 0x90000)
+    a.pos_key.stride[3] = 1 << 23              # 511 * 2^23 > 2^31
+    assert lib.vf_deberta_attention_fwd(ctypes.byref(a), None) == _lib.VF_EUNSUPPORTED

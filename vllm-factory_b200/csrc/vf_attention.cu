@@ -861,6 +861,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
                                        (long long)row0 * p.pq_sn
                                  : zero;
           const long long pq_sn = pq_on ? p.pq_sn : 0, pq_sk = pq_on ? p.pq_sk : 0;
+          // Offsets inside the tile are 32-bit (the host bounds them): a 64-bit address per
+          // column was 16-23 % slower.  n >= k0 for every column of a visited tile.
+          const T* pq_tile = pq_bh + (long long)k0 * pq_sn;
+          const int pq_sn32 = static_cast<int>(pq_sn), pq_sk32 = static_cast<int>(pq_sk), pk_sk32 = static_cast<int>(pk_sk);
           // S first (one TMEM read, so QK of the next tile can start), then the terms.
           tmem_ld_2x64_f2(tS, x2);
           tc_fence_before();
@@ -872,7 +876,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           for (int c = 0; c < kBN; ++c) {
             const int n = min(k0 + c, klen - 1);   // keys past klen are masked below
             const int idx = lut_s[min(max(m - n, -R), R) + R];
-            const float add = to_f<T>(pk_row[idx * pk_sk]) + to_f<T>(pq_bh[(long long)n * pq_sn + idx * pq_sk]);
+            const float add = to_f<T>(pk_row[idx * pk_sk32]) + to_f<T>(pq_tile[(n - k0) * pq_sn32 + idx * pq_sk32]);
             if (c & 1) x2[c >> 1].y = (x2[c >> 1].y + add) * scale_log2;
             else x2[c >> 1].x = (x2[c >> 1].x + add) * scale_log2;
           }
@@ -1342,6 +1346,15 @@ int deberta_prepare(const vf_deberta_attention_args_t* a, int64_t batch, vf::KPa
   const int span = a->position_buckets > 0 ? a->position_buckets : a->max_relative_distance;
   const bool has_pos = a->pos_key.data != nullptr || a->pos_query.data != nullptr;
   if (has_pos && span <= 0) return fail(VF_EINVAL, "deberta attention: position terms need position_buckets or max_relative_distance > 0");
+  // The kernel gathers a pos_key row with 32-bit offsets idx * stride (idx < 2 * span) and a
+  // key tile of pos_query with (n - k0) * row stride + idx * stride.
+  if (a->pos_key.data != nullptr &&
+      (a->pos_key.stride[3] < 0 || (2LL * span - 1) * a->pos_key.stride[3] >= (1LL << 31)))
+    return fail(VF_EUNSUPPORTED, "deberta attention: pos_key index stride too large for 32-bit offsets");
+  if (a->pos_query.data != nullptr &&
+      (a->pos_query.stride[2] < 0 || a->pos_query.stride[3] < 0 ||
+       (vf::kBN - 1LL) * a->pos_query.stride[2] + (2LL * span - 1) * a->pos_query.stride[3] >= (1LL << 31)))
+    return fail(VF_EUNSUPPORTED, "deberta attention: pos_query strides too large for 32-bit in-tile offsets");
   std::memset(kp, 0, offsetof(vf::KParams, lut));
   if ((rc = make_tile_map(&kp->tm_q, a->q, a->dtype, "q"))) return rc;
   if ((rc = make_tile_map(&kp->tm_k, a->k, a->dtype, "k"))) return rc;

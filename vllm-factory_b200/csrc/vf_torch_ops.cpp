@@ -76,6 +76,10 @@ at::Tensor to_kernel_dtype(const at::Tensor& t) {
   return at::clamp(t, -65504.0, 65504.0).to(at::kHalf);
 }
 
+// Position tensors are gathered along their last dimension with 32-bit offsets: give them
+// a unit last-dimension stride (row strides stay as they are).
+at::Tensor unit_last(const at::Tensor& t) { return t.stride(-1) == 1 ? t : t.contiguous(); }
+
 at::Tensor rpb_attention(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
                          const std::optional<at::Tensor>& rpb_table, int64_t num_buckets,
                          int64_t max_distance, bool is_decoder,
@@ -233,13 +237,13 @@ at::Tensor deberta_attention(const at::Tensor& q_in, const at::Tensor& k_in, con
   if (pos_key.has_value()) {
     require_cuda(*pos_key, "pos_key");
     TORCH_CHECK(pos_key->scalar_type() == q_in.scalar_type(), "vf_b200: pos_key must have the dtype of q");
-    pk = to_kernel_dtype(*pos_key);
+    pk = unit_last(to_kernel_dtype(*pos_key));
     a.pos_key = view4(pk);
   }
   if (pos_query.has_value()) {
     require_cuda(*pos_query, "pos_query");
     TORCH_CHECK(pos_query->scalar_type() == q_in.scalar_type(), "vf_b200: pos_query must have the dtype of q");
-    pq = to_kernel_dtype(*pos_query);
+    pq = unit_last(to_kernel_dtype(*pos_query));
     a.pos_query = view4(pq);
   }
   a.causal = causal ? 1 : 0;
@@ -281,14 +285,14 @@ at::Tensor deberta_attention_varlen(const at::Tensor& q_in, const at::Tensor& k_
     require_cuda(*pos_key, "pos_key");
     TORCH_CHECK(pos_key->dim() == 3, "vf_b200: packed pos_key must be [total, heads, 2*span]");
     TORCH_CHECK(pos_key->scalar_type() == q_in.scalar_type(), "vf_b200: pos_key must have the dtype of q");
-    pk = to_kernel_dtype(*pos_key);
+    pk = unit_last(to_kernel_dtype(*pos_key));
     a.pos_key = packed_view(pk);
   }
   if (pos_query.has_value()) {
     require_cuda(*pos_query, "pos_query");
     TORCH_CHECK(pos_query->dim() == 3, "vf_b200: packed pos_query must be [total, heads, 2*span]");
     TORCH_CHECK(pos_query->scalar_type() == q_in.scalar_type(), "vf_b200: pos_query must have the dtype of q");
-    pq = to_kernel_dtype(*pos_query);
+    pq = unit_last(to_kernel_dtype(*pos_query));
     a.pos_query = packed_view(pq);
   }
   a.causal = causal ? 1 : 0;
