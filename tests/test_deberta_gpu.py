@@ -166,3 +166,24 @@ def test_deberta_many_short_sequences_natural_order():
     lens = [(29 * b) % (L + 1) for b in range(B)]
     q, k, v, pk, pq, sl = make(B, 1, L, L, 32, lens=lens, seed=33)
     run(q, k, v, pk, pq, sl, sm_scale=0.125, pb=32, mr=64, log=True, what="1100 sequences")
+
+
+def test_deberta_position_views_strided_and_transposed():
+    """Position tensors as views: sliced out of wider tensors (large row strides, gathered in
+    place with 32-bit in-tile offsets) and with a non-unit last-dimension stride (the op
+    makes those contiguous first)."""
+    B, H, L, S = 2, 2, 300, 256
+    g = torch.Generator().manual_seed(41)
+    q, k, v = (torch.randn(B, H, L, 64, generator=g).to(torch.bfloat16) for _ in range(3))
+    wide_k = (torch.randn(B, H, L, 3 * S, generator=g) * 3).to(torch.bfloat16)
+    pk = wide_k[..., S:3 * S]                                  # row stride 3S, unit index stride
+    pq = (torch.randn(B, H, 2 * S, L, generator=g) * 3).to(torch.bfloat16).transpose(-1, -2)
+    sl = torch.tensor([300, 211], dtype=torch.int32)
+    sm = 1 / math.sqrt(64 * 3)
+    dev = torch.device("cuda")
+    pk_dev = wide_k.to(dev)[..., S:3 * S]                      # slice on the device: strides kept
+    assert pk_dev.stride(-2) == 3 * S and pq.to(dev).stride(-1) != 1
+    out = _op()(q.to(dev), k.to(dev), v.to(dev), sl.to(dev), pk_dev, pq.to(dev), False, sm, S, 512, True)
+    ref = oracle.deberta_attention_ref(q.float(), k.float(), v.float(), sl, pk.float(), pq.float(), False, sm, S,
+                                       512, True)
+    assert_close(out, ref, lens_mask(sl, L), what="strided / transposed position views")
