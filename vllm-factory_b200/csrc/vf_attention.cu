@@ -14,11 +14,12 @@
 // Warp roles (384 threads = 3 warpgroups):
 //   warps 0-3  softmax group 0 (query tile 0), one thread per query row
 //   warps 4-7  softmax group 1 (query tile 1)
-//   warp  8    TMA producer (Q per unit, double-buffered; a 3-stage K/V ring across units)
+//   warp  8    TMA producer (Q per unit and a K/V ring across units; depths per variant, Smem<>)
 //   warp  9    UMMA issuer (one elected lane) + TMEM allocation
 //   warp  10   unit preparation (schedule, live key span, per-head bias table), one unit ahead
 //   warp  11   UMMA issuer for group 1 (warp 9 then serves group 0)
-// Register split after the prologue: see kRegsSoftmax / kRegsProducer.
+// Register split after the prologue: kRegsSoftmax / kRegsProducer (T5), kRegsSoftmaxDeberta /
+// kRegsProducerDeberta.
 // TMEM (512 columns, fp32): per query tile g, S at 256g, P (bf16 pairs) at 256g+128,
 // O at 256g+192.  S = Q K^T and O += P V run on tcgen05.mma (kind::f16, fp32 accumulate);
 // softmax threads read S with tcgen05.ld, write P back with tcgen05.st, and the PV MMA
