@@ -863,8 +863,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
                                  : zero;
           const long long pq_sn = pq_on ? p.pq_sn : 0, pq_sk = pq_on ? p.pq_sk : 0;
           // Offsets inside the tile are 32-bit (the host bounds them): a 64-bit address per
-          // column was 16-23 % slower.  n >= k0 for every column of a visited tile.
+          // column was 16-23 % slower.  Per column only nn = min(c, klen - 1 - k0) varies
+          // (k0 < klen for every visited tile); the row and tile constants are hoisted, which
+          // took C1 from 84 to 72 us.
           const T* pq_tile = pq_bh + (long long)k0 * pq_sn;
+          const int nlim = klen - 1 - k0, mk = m - k0;
           const int pq_sn32 = static_cast<int>(pq_sn), pq_sk32 = static_cast<int>(pq_sk), pk_sk32 = static_cast<int>(pk_sk);
           // S first (one TMEM read, so QK of the next tile can start), then the terms.
           tmem_ld_2x64_f2(tS, x2);
@@ -875,9 +878,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           // the select kept both paths in the unrolled loop.)
 #pragma unroll
           for (int c = 0; c < kBN; ++c) {
-            const int n = min(k0 + c, klen - 1);   // keys past klen are masked below
-            const int idx = lut_s[min(max(m - n, -R), R) + R];
-            const float add = to_f<T>(pk_row[idx * pk_sk32]) + to_f<T>(pq_tile[(n - k0) * pq_sn32 + idx * pq_sk32]);
+            const int nn = min(c, nlim);            // key n = k0 + nn; keys past klen are masked below
+            const int idx = lut_s[min(max(mk - nn, -R), R) + R];
+            const float add = to_f<T>(pk_row[idx * pk_sk32]) + to_f<T>(pq_tile[nn * pq_sn32 + idx * pq_sk32]);
             if (c & 1) x2[c >> 1].y = (x2[c >> 1].y + add) * scale_log2;
             else x2[c >> 1].x = (x2[c >> 1].x + add) * scale_log2;
           }
