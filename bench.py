@@ -22,7 +22,9 @@ oracle port) on rank 0 and prints the same metric.
 Other workloads (`--workload`): deberta_c1 / deberta_c1_fp32 / deberta_c5_<L> (DeBERTa
 attention), mt5_c2_varlen / deberta_c1_varlen (packed batches), and the encoder stacks
 deberta_c3 / mt5_c4: a 256-sequence packed batch partitioned by sequence over the ranks
-(LPT on estimated FLOPs, strong scaling), 24 layers per step, value = encoder tokens/s.
+(LPT on estimated FLOPs, strong scaling), 24 layers per step, value = encoder tokens/s;
+mt5_ffn_act / deberta_add_ln: the HBM-bound ops beside the path (the mT5 gated-GELU, the
+DeBERTa residual add + LayerNorm), value = GB/s.
 """
 from __future__ import annotations
 
@@ -281,7 +283,8 @@ def encoder_cpu_baseline(name: str, budget_s: float = 15.0):
     else:
         fn = lambda q, k, v, cu, ms, t, nb, md, dec, sc: oracle.rpb_attention_varlen_ref(
             q, k, v, cu, t, nb, md, dec, sc, dtype=torch.float32)
-    extra = {} if name == "deberta_c3" else {"gated_act": lambda g, u, a: oracle.gated_act_ref(g, u, 0)}
+    extra = ({"add_norm": lambda x, r, w, b, eps: oracle.add_layer_norm_ref(x, r, w, b, eps)} if name == "deberta_c3"
+             else {"gated_act": lambda g, u, a: oracle.gated_act_ref(g, u, 0)})
     model = cls(small, device="cpu", dtype=torch.float32, seed=0, attention_fn=fn, **extra)
     done, n, t0 = 0, 0, time.perf_counter()
     while time.perf_counter() - t0 < budget_s and n < len(lengths):
@@ -399,19 +402,30 @@ def gated_act_cpu_baseline(budget_s: float = 10.0):
             "kind": "port", "sample": f"{n} x 2048 rows of the 16384 x 2816 workload, fp32 torch on CPU (oracle)"}
 
 
-def run_gated_act(args, world: int, rank: int, dev, warmup: int):
-    """mt5_ffn_act: the gated-GELU of one mT5-large FFN (kernels.ff_fused drop-in) on the
-    two halves of a stacked [16384, 2 x 2816] bf16 projection, read in place.  HBM-bound:
-    value = bytes moved (gate + up read, out written) / time, in GB/s."""
-    from kernels.ff_fused import fused_gelu_mul_dropout
-    T, Fd = 16384, 2816
-    g = torch.Generator(device=dev).manual_seed(4000 + rank)
-    sets = [(torch.randn(T, 2 * Fd, generator=g, device=dev) * 2).to(torch.bfloat16) for _ in range(3)]
-    nbytes = 3 * T * Fd * 2
+def add_layer_norm_cpu_baseline(budget_s: float = 10.0):
+    """The oracle of the reference's two calls (float64 torch) on the host cores over a
+    2048-row slice of the workload, repeated for ~10 s: GB/s of the same bytes."""
+    import oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(5000)
+    x, r = (torch.randn(2048, 1024, generator=g).to(torch.bfloat16) for _ in range(2))
+    w, b = torch.ones(1024, dtype=torch.bfloat16), torch.zeros(1024, dtype=torch.bfloat16)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        oracle.add_layer_norm_ref(x, r, w, b, 1e-7)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n * 3 * 2048 * 1024 * 2 / dt / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{n} x 2048 rows of the 65536 x 1024 workload, float64 torch on CPU (oracle)"}
+
+
+def _run_hbm_op(args, world: int, rank: int, dev, warmup: int, sets, call, nbytes: int, cfg: dict, cpu_fn):
+    """Shared timing of the HBM-bound elementwise ops: `call(*sets[i % len(sets)])` per
+    step; value = algorithmic bytes / time (GB/s).  e2e: the first input set from pinned
+    host memory in, the result out, every step."""
     stream = torch.cuda.current_stream(dev)
-    call = lambda gu: fused_gelu_mul_dropout(gu[:, :Fd], gu[:, Fd:], "gelu_new")
     for i in range(warmup):
-        call(sets[i % 3])
+        call(*sets[i % len(sets)])
     torch.cuda.synchronize()
     sampler = ClockSampler(dev.index or 0)
     sampler.start()
@@ -421,7 +435,7 @@ def run_gated_act(args, world: int, rank: int, dev, warmup: int):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for i in range(args.steps):
-        call(sets[i % 3])
+        call(*sets[i % len(sets)])
     ev1.record(stream)
     torch.cuda.synchronize()
     clocks = sampler.stop()
@@ -431,33 +445,63 @@ def run_gated_act(args, world: int, rank: int, dev, warmup: int):
     value = bytes_all * args.steps / (ms_max * 1e-3) / 1e9
     e2e = None
     if not args.no_e2e:
-        host = sets[0].cpu().pin_memory()
-        out_host = torch.empty(T, Fd, dtype=torch.bfloat16).pin_memory()
+        host = tuple(t.cpu().pin_memory() for t in sets[0])
+        out0 = call(*sets[0])
+        out_host = torch.empty(out0.shape, dtype=out0.dtype).pin_memory()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         n_e2e = max(3, min(args.steps, 10))
         e0.record(stream)
         for _ in range(n_e2e):
-            out_host.copy_(call(host.to(dev, non_blocking=True)), non_blocking=True)
+            out_host.copy_(call(*(t.to(dev, non_blocking=True) for t in host)), non_blocking=True)
         e1.record(stream)
         torch.cuda.synchronize()
         ems, _, _ = VD.reduce_timing(e0.elapsed_time(e1), 0.0, 0.0, dev)
         e2e = {"value": bytes_all * n_e2e / (ems * 1e-3) / 1e9, "unit": "GB/s",
-               "h2d_bytes_per_step": int(host.numel() * 2), "d2h_bytes_per_step": int(out_host.numel() * 2),
-               "steps": n_e2e}
+               "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in host)),
+               "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()), "steps": n_e2e}
     if rank != 0:
         return None
     peaks = measured_peaks()
     achieved = nbytes / (ms / args.steps * 1e-3) / 1e9
     return {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "mT5-large FFN gated-GELU (kernels/ff_fused.py drop-in), 16384 x 2816, halves of a stacked projection",
-                       "l2": "3 rotating 185 MB input sets > L2; no flush"},
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks.get("hbm", 6650.0), "unit": "GB/s",
                          "frac": achieved / peaks.get("hbm", 6650.0), "traffic": committed_traffic(args.workload),
                          "peak_source": f"{peaks['source']} HBM copy", "algorithmic_bytes_per_launch": nbytes},
             "gpu_launches": args.steps, "clocks": clocks, "e2e": e2e,
-            **({"cpu_baseline": gated_act_cpu_baseline()} if world == 1 and not args.no_cpu_baseline else {})}
+            **({"cpu_baseline": cpu_fn()} if world == 1 and not args.no_cpu_baseline else {})}
+
+
+def run_gated_act(args, world: int, rank: int, dev, warmup: int):
+    """mt5_ffn_act: the gated-GELU of one mT5-large FFN (kernels.ff_fused drop-in) on the
+    two halves of a stacked [16384, 2 x 2816] bf16 projection, read in place.  HBM-bound:
+    value = bytes moved (gate + up read, out written) / time, in GB/s."""
+    from kernels.ff_fused import fused_gelu_mul_dropout
+    T, Fd = 16384, 2816
+    g = torch.Generator(device=dev).manual_seed(4000 + rank)
+    sets = [((torch.randn(T, 2 * Fd, generator=g, device=dev) * 2).to(torch.bfloat16),) for _ in range(3)]
+    call = lambda gu: fused_gelu_mul_dropout(gu[:, :Fd], gu[:, Fd:], "gelu_new")
+    cfg = {"workload": "mT5-large FFN gated-GELU (kernels/ff_fused.py drop-in), 16384 x 2816, halves of a stacked projection",
+           "l2": "3 rotating 185 MB input sets > L2; no flush"}
+    return _run_hbm_op(args, world, rank, dev, warmup, sets, call, 3 * T * Fd * 2, cfg, gated_act_cpu_baseline)
+
+
+def run_add_layer_norm(args, world: int, rank: int, dev, warmup: int):
+    """deberta_add_ln: LayerNorm(x + residual) of a DeBERTa-v3-large layer output
+    (kernels.fused_add_layernorm drop-in for deberta_v2_encoder.py:507 / :566) over 65536
+    packed tokens x 1024, bf16.  HBM-bound: value = bytes moved (x, residual read, out
+    written) / time, in GB/s."""
+    from kernels.fused_add_layernorm import fused_add_layer_norm
+    T, E = 65536, 1024
+    g = torch.Generator(device=dev).manual_seed(5000 + rank)
+    sets = [tuple(torch.randn(T, E, generator=g, device=dev).to(torch.bfloat16) for _ in range(2)) for _ in range(2)]
+    w = (1.0 + 0.1 * torch.randn(E, generator=g, device=dev)).to(torch.bfloat16)
+    b = (0.1 * torch.randn(E, generator=g, device=dev)).to(torch.bfloat16)
+    call = lambda x, r: fused_add_layer_norm(x, r, w, b, 1e-7)
+    cfg = {"workload": "DeBERTa-v3-large residual add + LayerNorm (kernels/fused_add_layernorm.py), 65536 x 1024",
+           "l2": "2 rotating 256 MB input sets > L2; no flush"}
+    return _run_hbm_op(args, world, rank, dev, warmup, sets, call, 3 * T * E * 2, cfg, add_layer_norm_cpu_baseline)
 
 
 # ----------------------------------------------------------------------------- main
@@ -484,6 +528,8 @@ def main():
             cb = encoder_cpu_baseline(args.workload)
         elif args.workload == "mt5_ffn_act":
             cb = gated_act_cpu_baseline()
+        elif args.workload == "deberta_add_ln":
+            cb = add_layer_norm_cpu_baseline()
         else:
             cb = cpu_baseline(args.workload, None, budget_s=max(5.0, min(60.0, 2.0 * args.steps)))
         line = {"metric": METRIC, "value": cb["value"], "unit": cb["unit"], "n_gpus": args.gpus, "steps": args.steps,
@@ -507,8 +553,8 @@ def main():
     import vf_b200
     vf_b200.load()
 
-    if args.workload in ENCODER_WORKLOADS or args.workload == "mt5_ffn_act":
-        runner = run_gated_act if args.workload == "mt5_ffn_act" else run_encoder
+    if args.workload in ENCODER_WORKLOADS or args.workload in ("mt5_ffn_act", "deberta_add_ln"):
+        runner = {"mt5_ffn_act": run_gated_act, "deberta_add_ln": run_add_layer_norm}.get(args.workload, run_encoder)
         line = runner(args, world, rank, dev, warmup)
         if line is not None:
             print(json.dumps(line))

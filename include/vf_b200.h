@@ -162,6 +162,31 @@ typedef struct {
 int vf_gated_act_fwd(const vf_gated_act_args_t* args, void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * Residual add + LayerNorm of the DeBERTa-v2 encoder: out = LayerNorm(x + residual) with
+ * weight and bias over the last dimension.  Replaces the two torch kernels of
+ * models/deberta_v2/deberta_v2_encoder.py:507 and :566 (`self.LayerNorm(hidden_states +
+ * input_tensor)`, nn.LayerNorm) -- a torch call in the reference, not a kernel of its own.
+ * The sum is rounded to the dtype (as the reference's tensor add stores it); mean, biased
+ * variance and the affine map in fp32; result rounded to the dtype.
+ * x, residual, out: rows x cols views of one dtype (f32/f16/bf16), unit column stride, row
+ * strides in elements (>= cols); out must not overlap x or residual.  weight, bias: [cols]
+ * of the same dtype; bias may be NULL (zero).  eps: finite, >= 0.
+ * ------------------------------------------------------------------------------------ */
+typedef struct {
+  vf_dtype_t dtype;
+  const void* x;
+  const void* residual;
+  const void* weight;
+  const void* bias;
+  void* out;
+  int64_t rows, cols;
+  int64_t x_row_stride, residual_row_stride, out_row_stride;
+  float eps;
+} vf_add_layer_norm_args_t;
+
+int vf_add_layer_norm_fwd(const vf_add_layer_norm_args_t* args, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Host-side bucket functions (no GPU needed).  These are the exact integer outputs the
  * kernels use; they restate, in float32 arithmetic like the reference's torch code:
  *  - models/mt5/mt5_encoder.py:125 T5RelativePositionBias._relative_position_bucket

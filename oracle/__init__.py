@@ -34,3 +34,4 @@ from .rpb import (  # noqa: F401
     t5_relative_bucket_ref,
 )
 from .ffn import gated_act_ref  # noqa: F401,E402
+from .layernorm import add_layer_norm_ref  # noqa: F401,E402

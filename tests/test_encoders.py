@@ -37,7 +37,8 @@ def _packing_invariance(model, vocab):
 def test_deberta_encoder_packing_invariance():
     cfg = dataclasses.replace(EN.DebertaConfig(), layers=2, hidden=128, heads=2, ffn=256, vocab=500,
                               position_buckets=16, max_relative_positions=64)
-    _packing_invariance(EN.DebertaV3Encoder(cfg, device="cpu", dtype=torch.float32, attention_fn=_deb_attn), 500)
+    _packing_invariance(EN.DebertaV3Encoder(cfg, device="cpu", dtype=torch.float32, attention_fn=_deb_attn,
+                                            add_norm=EN.add_layer_norm_torch), 500)
 
 
 def test_mt5_encoder_packing_invariance():
@@ -56,7 +57,8 @@ def test_deberta_position_scores_are_q_dot_kr():
         seen.update(q=q, k=k, pk=pk, pq=pq)
         return _deb_attn(q, k, v, cu, ms, pk, pq, *rest)
 
-    m = EN.DebertaV3Encoder(cfg, device="cpu", dtype=torch.float32, attention_fn=spy)
+    m = EN.DebertaV3Encoder(cfg, device="cpu", dtype=torch.float32, attention_fn=spy,
+                            add_norm=EN.add_layer_norm_torch)
     lengths, ids = EN.packed_batch(2, 5, 9, 100, seed=2)
     x, cu, lens = EN.select_sequences(lengths, ids, range(2))
     m.forward(x, cu, max(lens))

@@ -24,6 +24,10 @@ def test_meta_shapes_and_dtypes(dtype):
     g = torch.empty(5, 7, 2816, **m)
     o = OPS.gated_act(g, g, 0)
     assert o.shape == g.shape and o.dtype == dtype
+    h = torch.empty(5, 7, 1024, **m)
+    w = torch.empty(1024, **m)
+    o = OPS.add_layer_norm(h, h, w, w, 1e-7)
+    assert o.shape == h.shape and o.dtype == dtype
 
 
 def test_cpu_tensors_raise():
@@ -34,6 +38,7 @@ def test_cpu_tensors_raise():
                  lambda: OPS.deberta_attention(q, q, q, None, None, None, False, None, 256, 512, True),
                  lambda: OPS.rpb_attention_varlen(qp, qp, qp, cu, 8, None, 32, 128, False, 1.0),
                  lambda: OPS.deberta_attention_varlen(qp, qp, qp, cu, 8, None, None, False, None, 256, 512, True),
-                 lambda: OPS.gated_act(q, q, 0)):
+                 lambda: OPS.gated_act(q, q, 0),
+                 lambda: OPS.add_layer_norm(qp, qp, qp[0, 0], None, 1e-7)):
         with pytest.raises(RuntimeError, match="CUDA"):
             call()

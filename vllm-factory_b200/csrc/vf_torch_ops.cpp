@@ -311,6 +311,22 @@ at::Tensor deberta_attention_varlen(const at::Tensor& q_in, const at::Tensor& k_
 // rows.  Each operand only needs a unit stride on the last dimension and leading
 // dimensions that collapse to one row stride (as the two column halves of a 2-D [T, 2F]
 // projection do); anything else is copied contiguous first.
+// A 2-D (rows, cols) view of t with unit column stride, without a copy when possible.
+at::Tensor as_rows(const at::Tensor& t, int64_t rows, int64_t cols) {
+  at::Tensor x = t;
+  if (x.dim() == 1) x = x.unsqueeze(0);
+  if (x.stride(-1) != 1) x = x.contiguous();
+  if (x.dim() > 2) {
+    bool collapses = true;   // leading dims form one row stride
+    for (int64_t d = x.dim() - 2; d > 0; --d)
+      if (x.size(d - 1) > 1 && x.stride(d - 1) != x.stride(d) * x.size(d)) collapses = false;
+    if (!collapses) x = x.contiguous();
+    x = x.reshape({rows, cols});
+  }
+  if (x.size(0) > 1 && x.stride(0) < cols) x = x.contiguous();   // overlapping or broadcast rows
+  return x;
+}
+
 at::Tensor gated_act(const at::Tensor& gate_in, const at::Tensor& up_in, int64_t act) {
   require_cuda(gate_in, "gate");
   require_cuda(up_in, "up");
@@ -320,22 +336,7 @@ at::Tensor gated_act(const at::Tensor& gate_in, const at::Tensor& up_in, int64_t
   c10::cuda::CUDAGuard guard(gate_in.device());
   const int64_t cols = gate_in.size(-1);
   const int64_t rows = cols == 0 ? 0 : gate_in.numel() / cols;
-  // A 2-D (rows, cols) view with unit column stride, without a copy when possible.
-  auto as_rows = [&](const at::Tensor& t) {
-    at::Tensor x = t;
-    if (x.dim() == 1) x = x.unsqueeze(0);
-    if (x.stride(-1) != 1) x = x.contiguous();
-    if (x.dim() > 2) {
-      bool collapses = true;   // leading dims form one row stride
-      for (int64_t d = x.dim() - 2; d > 0; --d)
-        if (x.size(d - 1) > 1 && x.stride(d - 1) != x.stride(d) * x.size(d)) collapses = false;
-      if (!collapses) x = x.contiguous();
-      x = x.reshape({rows, cols});
-    }
-    if (x.size(0) > 1 && x.stride(0) < cols) x = x.contiguous();   // overlapping or broadcast rows
-    return x;
-  };
-  const at::Tensor g = as_rows(gate_in), u = as_rows(up_in);
+  const at::Tensor g = as_rows(gate_in, rows, cols), u = as_rows(up_in, rows, cols);
   at::Tensor out = at::empty(gate_in.sizes(), gate_in.options());
   if (rows == 0 || cols == 0) return out;
   vf_gated_act_args_t a{};
@@ -356,6 +357,56 @@ at::Tensor gated_act(const at::Tensor& gate_in, const at::Tensor& up_in, int64_t
 at::Tensor gated_act_meta(const at::Tensor& gate, const at::Tensor&, int64_t) { return at::empty_like(gate); }
 at::Tensor gated_act_cpu(const at::Tensor&, const at::Tensor&, int64_t) {
   TORCH_CHECK(false, "vf_b200: gate and up must be CUDA tensors (no CPU implementation)");
+}
+
+// out = LayerNorm(x + residual) over the last dimension (weight, optional bias), one pass.
+at::Tensor add_layer_norm(const at::Tensor& x_in, const at::Tensor& res_in, const at::Tensor& weight_in,
+                          const std::optional<at::Tensor>& bias_in, double eps) {
+  require_cuda(x_in, "x");
+  require_cuda(res_in, "residual");
+  require_cuda(weight_in, "weight");
+  TORCH_CHECK(x_in.sizes() == res_in.sizes(), "vf_b200: x and residual must have identical shapes");
+  TORCH_CHECK(x_in.dim() >= 1, "vf_b200: x must have at least one dimension");
+  const int64_t cols = x_in.size(-1);
+  TORCH_CHECK(weight_in.dim() == 1 && weight_in.size(0) == cols, "vf_b200: weight must be [", cols, "]");
+  TORCH_CHECK(x_in.scalar_type() == res_in.scalar_type() && x_in.scalar_type() == weight_in.scalar_type(),
+              "vf_b200: x, residual and weight must share a dtype");
+  at::Tensor bias;
+  if (bias_in.has_value() && bias_in->defined()) {
+    require_cuda(*bias_in, "bias");
+    TORCH_CHECK(bias_in->dim() == 1 && bias_in->size(0) == cols, "vf_b200: bias must be [", cols, "]");
+    TORCH_CHECK(bias_in->scalar_type() == x_in.scalar_type(), "vf_b200: bias must share the dtype of x");
+    bias = bias_in->contiguous();
+  }
+  c10::cuda::CUDAGuard guard(x_in.device());
+  const int64_t rows = cols == 0 ? 0 : x_in.numel() / cols;
+  at::Tensor out = at::empty(x_in.sizes(), x_in.options());
+  if (rows == 0 || cols == 0) return out;
+  const at::Tensor x = as_rows(x_in, rows, cols), r = as_rows(res_in, rows, cols), w = weight_in.contiguous();
+  vf_add_layer_norm_args_t a{};
+  a.dtype = dtype_code(x);
+  a.x = x.data_ptr();
+  a.residual = r.data_ptr();
+  a.weight = w.data_ptr();
+  a.bias = bias.defined() ? bias.data_ptr() : nullptr;
+  a.out = out.data_ptr();
+  a.rows = rows;
+  a.cols = cols;
+  a.x_row_stride = rows > 1 ? x.stride(0) : cols;
+  a.residual_row_stride = rows > 1 ? r.stride(0) : cols;
+  a.out_row_stride = cols;
+  a.eps = static_cast<float>(eps);
+  check_rc(vf_add_layer_norm_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
+  return out;
+}
+
+at::Tensor add_layer_norm_meta(const at::Tensor& x, const at::Tensor&, const at::Tensor&,
+                               const std::optional<at::Tensor>&, double) {
+  return at::empty_like(x);
+}
+at::Tensor add_layer_norm_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                              const std::optional<at::Tensor>&, double) {
+  TORCH_CHECK(false, "vf_b200: x and residual must be CUDA tensors (no CPU implementation)");
 }
 
 // Shape functions for tracing (torch.compile / fake tensors).
@@ -414,6 +465,7 @@ TORCH_LIBRARY(vf_b200, m) {
         "Tensor? pos_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "
         "bool use_log_bucket) -> Tensor");
   m.def("gated_act(Tensor gate, Tensor up, int act) -> Tensor");
+  m.def("add_layer_norm(Tensor x, Tensor residual, Tensor weight, Tensor? bias, float eps) -> Tensor");
   m.def("deberta_attention_varlen(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, int max_seqlen, Tensor? pos_key, "
         "Tensor? pos_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "
         "bool use_log_bucket) -> Tensor");
@@ -425,6 +477,7 @@ TORCH_LIBRARY_IMPL(vf_b200, CUDA, m) {
   m.impl("deberta_attention", &deberta_attention);
   m.impl("deberta_attention_varlen", &deberta_attention_varlen);
   m.impl("gated_act", &gated_act);
+  m.impl("add_layer_norm", &add_layer_norm);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
@@ -433,6 +486,7 @@ TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
   m.impl("deberta_attention", &deberta_attention_cpu);
   m.impl("deberta_attention_varlen", &deberta_attention_varlen_cpu);
   m.impl("gated_act", &gated_act_cpu);
+  m.impl("add_layer_norm", &add_layer_norm_cpu);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
@@ -441,4 +495,5 @@ TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
   m.impl("deberta_attention", &deberta_attention_meta);
   m.impl("deberta_attention_varlen", &deberta_attention_varlen_meta);
   m.impl("gated_act", &gated_act_meta);
+  m.impl("add_layer_norm", &add_layer_norm_meta);
 }

@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "vf_deberta_attention_fwd",
     "vf_deberta_attention_varlen_fwd",
     "vf_gated_act_fwd",
+    "vf_add_layer_norm_fwd",
     "vf_t5_relative_bucket",
     "vf_deberta_log_bucket",
     "vf_last_error",
@@ -87,6 +88,23 @@ class GatedActArgs(ctypes.Structure):
         ("up_row_stride", ctypes.c_int64),
         ("out_row_stride", ctypes.c_int64),
         ("act", ctypes.c_int32),
+    ]
+
+
+class AddLayerNormArgs(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_int),
+        ("x", ctypes.c_void_p),
+        ("residual", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+        ("x_row_stride", ctypes.c_int64),
+        ("residual_row_stride", ctypes.c_int64),
+        ("out_row_stride", ctypes.c_int64),
+        ("eps", ctypes.c_float),
     ]
 
 
@@ -146,6 +164,8 @@ def load() -> ctypes.CDLL:
         lib.vf_deberta_attention_varlen_fwd.restype = ctypes.c_int
         lib.vf_gated_act_fwd.argtypes = [ctypes.POINTER(GatedActArgs), ctypes.c_void_p]
         lib.vf_gated_act_fwd.restype = ctypes.c_int
+        lib.vf_add_layer_norm_fwd.argtypes = [ctypes.POINTER(AddLayerNormArgs), ctypes.c_void_p]
+        lib.vf_add_layer_norm_fwd.restype = ctypes.c_int
         lib.vf_t5_relative_bucket.argtypes = [ctypes.c_int32] * 5 + [ctypes.POINTER(ctypes.c_int32)]
         lib.vf_t5_relative_bucket.restype = ctypes.c_int
         lib.vf_deberta_log_bucket.argtypes = [ctypes.c_int32] * 4 + [ctypes.POINTER(ctypes.c_int32)]

@@ -8,7 +8,8 @@ stacks measure encoder tokens/s with the hot path in place:
   DebertaV3Encoder  models/deberta_v2/deberta_v2_encoder.py (DebertaV2 embeddings without
                     absolute positions, DisentangledSelfAttentionV2._flash_forward :246-328
                     with share_att_key, c2p|p2c, position_buckets 256 / max_relative 512,
-                    rel_embeddings + LayerNorm, GELU FFN, post-LayerNorm residuals).
+                    rel_embeddings + LayerNorm, GELU FFN, post-LayerNorm residuals through
+                    this package's fused_add_layer_norm as at :507 / :566).
   MT5Encoder        models/mt5/mt5_encoder.py (T5 RMS LayerNorm, no QK scaling, the bias
                     table of layer 0 shared by all layers :546-566, gated-GELU FFN with the
                     tanh GELU through this package's fused_gelu_mul_dropout as at :418,
@@ -63,6 +64,12 @@ def _layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float) -
     return F.layer_norm(x, (x.shape[-1],), w, b, eps)
 
 
+def add_layer_norm_torch(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, b: torch.Tensor,
+                         eps: float) -> torch.Tensor:
+    """The reference's two torch calls, LayerNorm(x + residual): the encoders' CPU form."""
+    return _layer_norm(x + residual, w, b, eps)
+
+
 def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     # T5LayerNorm (no mean subtraction, no bias) as torch's fused RMS norm, which keeps the
     # variance in fp32 for 16-bit inputs like models/mt5/mt5_encoder.py does
@@ -70,11 +77,12 @@ def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 
 
 class DebertaV3Encoder:
-    """DeBERTa-v3 encoder over a packed batch; attention = flash_deberta_attention_varlen
-    (or, with `attention_fn`, any function of the same signature, e.g. a CPU oracle)."""
+    """DeBERTa-v3 encoder over a packed batch; attention = flash_deberta_attention_varlen and
+    the residual add + LayerNorm = fused_add_layer_norm (or, with `attention_fn` / `add_norm`,
+    any function of the same signature, e.g. a CPU oracle)."""
 
     def __init__(self, cfg: DebertaConfig = DebertaConfig(), device="cuda", dtype=torch.bfloat16, seed: int = 0,
-                 attention_fn=None):
+                 attention_fn=None, add_norm=None):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         g = torch.Generator(device=self.device).manual_seed(seed)
         E, F_, S2 = cfg.hidden, cfg.ffn, 2 * cfg.position_buckets
@@ -96,6 +104,9 @@ class DebertaV3Encoder:
         if attention_fn is None:
             from kernels.flash_deberta_attention import flash_deberta_attention_varlen as attention_fn
         self.attention_fn = attention_fn
+        if add_norm is None:
+            from kernels.fused_add_layernorm import fused_add_layer_norm as add_norm
+        self.add_norm = add_norm
 
     @torch.no_grad()
     def forward(self, ids: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
@@ -115,9 +126,9 @@ class DebertaV3Encoder:
             ctx = self.attention_fn(q, k, v, cu_seqlens, max_seqlen, pos_key, pos_query, False, sm_scale,
                                     cfg.position_buckets, cfg.max_relative_positions, True)
             a = torch.addmm(L["bo"], ctx.reshape(T, E).to(h.dtype), L["wo"].t())
-            h = _layer_norm(a + h, *L["ln1"], cfg.eps)
+            h = self.add_norm(a, h, *L["ln1"], cfg.eps)
             f = F.gelu(torch.addmm(L["b1"], h, L["w1"].t()))
-            h = _layer_norm(torch.addmm(L["b2"], f, L["w2"].t()) + h, *L["ln2"], cfg.eps)
+            h = self.add_norm(torch.addmm(L["b2"], f, L["w2"].t()), h, *L["ln2"], cfg.eps)
         return h
 
     def flops_per_token_gemm(self) -> float:

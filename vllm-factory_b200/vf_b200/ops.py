@@ -16,6 +16,7 @@ strides and the current CUDA stream and calls the C ABI of libvf_b200.so:
                                              max_relative_distance, use_log_bucket)   # packed
 
   torch.ops.vf_b200.gated_act(gate, up, act)                  # mT5 FFN: act(gate) * up
+  torch.ops.vf_b200.add_layer_norm(x, residual, w, b, eps)   # DeBERTa: LayerNorm(x + residual)
 
 All borrow their inputs (layouts TMA cannot describe are copied contiguous), allocate
 only the output, launch on the caller's stream, and have Meta implementations for
@@ -42,3 +43,4 @@ rpb_attention_varlen = torch.ops.vf_b200.rpb_attention_varlen
 deberta_attention = torch.ops.vf_b200.deberta_attention
 deberta_attention_varlen = torch.ops.vf_b200.deberta_attention_varlen
 gated_act = torch.ops.vf_b200.gated_act
+add_layer_norm = torch.ops.vf_b200.add_layer_norm
