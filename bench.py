@@ -421,11 +421,20 @@ def add_layer_norm_cpu_baseline(budget_s: float = 10.0):
 
 def _run_hbm_op(args, world: int, rank: int, dev, warmup: int, sets, call, nbytes: int, cfg: dict, cpu_fn):
     """Shared timing of the HBM-bound elementwise ops: `call(*sets[i % len(sets)])` per
-    step; value = algorithmic bytes / time (GB/s).  e2e: the first input set from pinned
-    host memory in, the result out, every step."""
+    step; value = algorithmic bytes / time (GB/s).  The host time of one op call (Python,
+    dispatch, output allocation) exceeds these kernels' device time, so the K timed steps
+    are captured once in a CUDA graph and the replay is timed: all K launches run, back to
+    back.  e2e: eager calls, the first input set from pinned host memory in, the result
+    out, every step."""
     stream = torch.cuda.current_stream(dev)
     for i in range(warmup):
         call(*sets[i % len(sets)])
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(args.steps):
+            call(*sets[i % len(sets)])
+    graph.replay()                                   # one untimed replay
     torch.cuda.synchronize()
     sampler = ClockSampler(dev.index or 0)
     sampler.start()
@@ -434,8 +443,7 @@ def _run_hbm_op(args, world: int, rank: int, dev, warmup: int, sets, call, nbyte
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for i in range(args.steps):
-        call(*sets[i % len(sets)])
+    graph.replay()
     ev1.record(stream)
     torch.cuda.synchronize()
     clocks = sampler.stop()
@@ -483,7 +491,7 @@ def run_gated_act(args, world: int, rank: int, dev, warmup: int):
     sets = [((torch.randn(T, 2 * Fd, generator=g, device=dev) * 2).to(torch.bfloat16),) for _ in range(3)]
     call = lambda gu: fused_gelu_mul_dropout(gu[:, :Fd], gu[:, Fd:], "gelu_new")
     cfg = {"workload": "mT5-large FFN gated-GELU (kernels/ff_fused.py drop-in), 16384 x 2816, halves of a stacked projection",
-           "l2": "3 rotating 185 MB input sets > L2; no flush"}
+           "l2": "3 rotating 185 MB input sets > L2; no flush", "launch": "K steps in one CUDA graph"}
     return _run_hbm_op(args, world, rank, dev, warmup, sets, call, 3 * T * Fd * 2, cfg, gated_act_cpu_baseline)
 
 
@@ -500,7 +508,7 @@ def run_add_layer_norm(args, world: int, rank: int, dev, warmup: int):
     b = (0.1 * torch.randn(E, generator=g, device=dev)).to(torch.bfloat16)
     call = lambda x, r: fused_add_layer_norm(x, r, w, b, 1e-7)
     cfg = {"workload": "DeBERTa-v3-large residual add + LayerNorm (kernels/fused_add_layernorm.py), 65536 x 1024",
-           "l2": "2 rotating 256 MB input sets > L2; no flush"}
+           "l2": "2 rotating 256 MB input sets > L2; no flush", "launch": "K steps in one CUDA graph"}
     return _run_hbm_op(args, world, rank, dev, warmup, sets, call, 3 * T * E * 2, cfg, add_layer_norm_cpu_baseline)
 
 

@@ -58,3 +58,14 @@ def test_deberta_padded_and_packed_in_graphs():
                                        for i, d in enumerate((64, 64, 64, 512, 512))),
                        lambda q, k, v, pk, pq: flash_deberta_attention_varlen(q, k, v, cu, 269, pk, pq, False, sm,
                                                                               256, 512, True))
+
+
+def test_gated_act_and_add_layer_norm_in_graphs():
+    """The two HBM-bound ops beside the path (bench.py times them as a captured graph)."""
+    from kernels.ff_fused import fused_gelu_mul_dropout
+    from kernels.fused_add_layernorm import fused_add_layer_norm
+    _capture_and_check(lambda s: (_rand(s, 300, 2 * 704, scale=2.0),),
+                       lambda gu: fused_gelu_mul_dropout(gu[:, :704], gu[:, 704:], "gelu_new"))
+    w, b = _rand(7, 1024) + 1.0, _rand(8, 1024, scale=0.1)
+    _capture_and_check(lambda s: (_rand(s, 513, 1024), _rand(s + 10, 513, 1024)),
+                       lambda x, r: fused_add_layer_norm(x, r, w, b, 1e-7))
