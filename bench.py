@@ -10,7 +10,8 @@ call of the drop-in `kernels.flash_attention_rpb.flash_attention_rpb_final` on t
                spans > 3x the 126 MB L2), so no step is served from L2.
   e2e          the same metric through the same public call with pinned HOST buffers:
                every step copies q, k, v, table and mask host->device and the output
-               device->host inside the timed region.
+               device->host inside the timed region; copies of neighbouring steps overlap
+               the compute (upload, compute and download streams, two device slots).
   roofline     dominant kernel vs the measured dense bf16 peak (MEASURED_PEAKS.json).
   cpu_baseline the oracle (CPU restatement of the reference's torch path) on this host.
 
@@ -65,6 +66,69 @@ def committed_traffic(workload: str):
         d = json.loads(p.read_text())
         return d.get(workload)
     return None
+
+
+def pipelined_e2e(dev, host: dict, call, n_steps: int, world: int):
+    """End-to-end time of `n_steps` calls through the public op with host buffers: every
+    step copies its inputs (the tensors of `host`, pinned) to the device and its result
+    back to pinned host memory, inside the timed region.  As a serving loop would, the
+    copies of neighbouring steps overlap the compute: uploads on one stream into two
+    device slots, compute on the current stream, downloads on a third; events order each
+    slot's upload after the compute that last read it, each compute after its upload and
+    each download after its compute.  Returns (max-over-ranks ms, h2d bytes, d2h bytes)."""
+    cur = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    keys = [k for k, v in host.items() if isinstance(v, torch.Tensor)]
+    slots = [{k: torch.empty(host[k].shape, dtype=host[k].dtype, device=dev) for k in keys} for _ in range(2)]
+    probe = call({**host, **{k: slots[0][k].copy_(host[k]) for k in keys}})
+    outs = [torch.empty(probe.shape, dtype=probe.dtype).pin_memory() for _ in range(2)]
+    torch.cuda.synchronize()
+    h2d = sum(host[k].numel() * host[k].element_size() for k in keys)
+    d2h = outs[0].numel() * outs[0].element_size()
+
+    def run(n):
+        done = [None, None]                        # compute event of the last step per slot
+        copied = [None, None]                      # download event of the last step per output
+        for i in range(n):
+            s = i % 2
+            with torch.cuda.stream(up):
+                if done[s] is not None:
+                    up.wait_event(done[s])
+                for k in keys:
+                    slots[s][k].copy_(host[k], non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(up)
+            cur.wait_event(ready)
+            o = call({**host, **slots[s]})
+            done[s] = torch.cuda.Event()
+            done[s].record(cur)
+            with torch.cuda.stream(down):
+                down.wait_event(done[s])
+                if copied[s] is not None:
+                    down.wait_event(copied[s])
+                outs[s].copy_(o, non_blocking=True)
+                o.record_stream(down)
+                copied[s] = torch.cuda.Event()
+                copied[s].record(down)
+        for ev in copied:
+            if ev is not None:
+                cur.wait_event(ev)
+
+    run(2)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    up.wait_event(e0)
+    down.wait_event(e0)
+    run(n_steps)
+    e1.record(cur)
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    return ms.item(), h2d, d2h
 
 
 class ClockSampler:
@@ -339,28 +403,12 @@ def run_encoder(args, world: int, rank: int, dev, warmup: int):
 
     e2e = None
     if not args.no_e2e:
-        ids_host, cu_host = x_ids.pin_memory(), cu.pin_memory()
-        out_host = torch.empty((x_ids.shape[0], cfg.hidden), dtype=torch.bfloat16).pin_memory()
-
-        def e2e_step():
-            o = model.forward(ids_host.to(dev, non_blocking=True), cu_host.to(dev, non_blocking=True), max_len)
-            out_host.copy_(o, non_blocking=True)
-
-        e2e_step()
-        torch.cuda.synchronize()
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        host = {"ids": x_ids.pin_memory(), "cu": cu.pin_memory()}
         n_e2e = max(3, min(args.steps, 10))
-        e0.record(stream)
-        for _ in range(n_e2e):
-            e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
+        ems, h2d, d2h = pipelined_e2e(dev, host, lambda x: model.forward(x["ids"], x["cu"], max_len), n_e2e, world)
         barrier()
-        ems, _, _ = VD.reduce_timing(e0.elapsed_time(e1), 0.0, 0.0, dev)
-        e2e = {"value": tokens_all * n_e2e / (ems * 1e-3), "unit": "tokens/s",
-               "h2d_bytes_per_step": int(ids_host.numel() * ids_host.element_size() + cu_host.numel() * 4),
-               "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()), "steps": n_e2e}
+        e2e = {"value": tokens_all * n_e2e / (ems * 1e-3), "unit": "tokens/s", "pipelined": True,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": n_e2e}
     if rank != 0:
         return None
     peaks = measured_peaks()
@@ -453,20 +501,11 @@ def _run_hbm_op(args, world: int, rank: int, dev, warmup: int, sets, call, nbyte
     value = bytes_all * args.steps / (ms_max * 1e-3) / 1e9
     e2e = None
     if not args.no_e2e:
-        host = tuple(t.cpu().pin_memory() for t in sets[0])
-        out0 = call(*sets[0])
-        out_host = torch.empty(out0.shape, dtype=out0.dtype).pin_memory()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        host = {str(j): t.cpu().pin_memory() for j, t in enumerate(sets[0])}
         n_e2e = max(3, min(args.steps, 10))
-        e0.record(stream)
-        for _ in range(n_e2e):
-            out_host.copy_(call(*(t.to(dev, non_blocking=True) for t in host)), non_blocking=True)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ems, _, _ = VD.reduce_timing(e0.elapsed_time(e1), 0.0, 0.0, dev)
-        e2e = {"value": bytes_all * n_e2e / (ems * 1e-3) / 1e9, "unit": "GB/s",
-               "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in host)),
-               "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()), "steps": n_e2e}
+        ems, h2d, d2h = pipelined_e2e(dev, host, lambda x: call(*(x[str(j)] for j in range(len(host)))), n_e2e, world)
+        e2e = {"value": bytes_all * n_e2e / (ems * 1e-3) / 1e9, "unit": "GB/s", "pipelined": True,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": n_e2e}
     if rank != 0:
         return None
     peaks = measured_peaks()
@@ -613,33 +652,11 @@ def main():
     if not args.no_e2e:
         host = {k: (v.cpu().pin_memory() if isinstance(v, torch.Tensor) and v.is_cuda and k in keys else v)
                 for k, v in sets[0].items()}
-        h2d = sum(v.numel() * v.element_size() for k, v in host.items() if k in keys and isinstance(v, torch.Tensor))
-        out_host = torch.empty(sets[0]["q"].shape, dtype=sets[0]["q"].dtype).pin_memory()
-        d2h = out_host.numel() * out_host.element_size()
-
-        def e2e_step():
-            x = {k: (v.to(dev, non_blocking=True) if k in keys and isinstance(v, torch.Tensor) else v)
-                 for k, v in host.items()}
-            o = call(x)
-            out_host.copy_(o, non_blocking=True)
-
-        for _ in range(2):
-            e2e_step()
-        torch.cuda.synchronize()
-        barrier()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
         n_e2e = max(3, min(args.steps, 30))
-        e0.record(stream)
-        for _ in range(n_e2e):
-            e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
+        ems, h2d, d2h = pipelined_e2e(dev, {k: v for k, v in host.items() if k in keys},
+                                      lambda x: call({**host, **x}), n_e2e, world)
         barrier()
-        ems = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-        if world > 1:
-            torch.distributed.all_reduce(ems, op=torch.distributed.ReduceOp.MAX)
-        e2e = {"value": flops_all * n_e2e / (ems.item() * 1e-3) / 1e12, "unit": "TFLOP/s",
+        e2e = {"value": flops_all * n_e2e / (ems * 1e-3) / 1e12, "unit": "TFLOP/s", "pipelined": True,
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": n_e2e}
 
     if world > 1:
