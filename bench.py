@@ -347,7 +347,8 @@ def encoder_cpu_baseline(name: str, budget_s: float = 15.0):
     else:
         fn = lambda q, k, v, cu, ms, t, nb, md, dec, sc: oracle.rpb_attention_varlen_ref(
             q, k, v, cu, t, nb, md, dec, sc, dtype=torch.float32)
-    extra = ({"add_norm": lambda x, r, w, b, eps: oracle.add_layer_norm_ref(x, r, w, b, eps)} if name == "deberta_c3"
+    extra = ({"add_norm": lambda x, r, w, b, eps: oracle.add_layer_norm_ref(x, r, w, b, eps),
+              "act_fn": lambda x: oracle.gated_act_ref(x, None, 1)} if name == "deberta_c3"
              else {"gated_act": lambda g, u, a: oracle.gated_act_ref(g, u, 0)})
     model = cls(small, device="cpu", dtype=torch.float32, seed=0, attention_fn=fn, **extra)
     done, n, t0 = 0, 0, time.perf_counter()

@@ -146,6 +146,9 @@ int vf_deberta_attention_varlen_fwd(const vf_deberta_attention_args_t* args, con
  * projection.  act: VF_ACT_GELU_TANH for 'gelu' / 'gelu_new' / 'gelu_fast' /
  * 'gelu_pytorch_tanh', VF_ACT_GELU_ERF for 'gelu_accurate', VF_ACT_RELU, VF_ACT_SILU
  * ('silu' / 'swish') -- the reference's _act_type_map (:77-85).
+ * up = NULL (up_row_stride ignored) computes the plain activation out = act(gate): the
+ * DeBERTa feed-forward's `intermediate_act_fn` (models/deberta_v2/deberta_v2_encoder.py,
+ * exact GELU), which the reference leaves to torch; no counterpart kernel there.
  * ------------------------------------------------------------------------------------ */
 enum { VF_ACT_GELU_TANH = 0, VF_ACT_GELU_ERF = 1, VF_ACT_RELU = 2, VF_ACT_SILU = 3 };
 

@@ -11,7 +11,9 @@ import torch
 ACT_GELU_TANH, ACT_GELU_ERF, ACT_RELU, ACT_SILU = 0, 1, 2, 3
 
 
-def gated_act_ref(gate: torch.Tensor, up: torch.Tensor, act: int = ACT_GELU_TANH) -> torch.Tensor:
+def gated_act_ref(gate: torch.Tensor, up, act: int = ACT_GELU_TANH) -> torch.Tensor:
+    """act(gate) * up in fp32, cast to gate's dtype; up = None gives act(gate) alone (the
+    DeBERTa feed-forward's activation, models/deberta_v2/deberta_v2_encoder.py)."""
     g = gate.float()
     if act == ACT_GELU_TANH:
         inner = 0.7978845834732056 * (g + 0.044715 * g * g * g)     # :48-51
@@ -22,4 +24,4 @@ def gated_act_ref(gate: torch.Tensor, up: torch.Tensor, act: int = ACT_GELU_TANH
         g = torch.clamp_min(g, 0.0)
     else:
         g = g * torch.sigmoid(g)
-    return (g * up.float()).to(gate.dtype)
+    return (g if up is None else g * up.float()).to(gate.dtype)

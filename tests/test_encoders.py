@@ -4,6 +4,7 @@ sequence partition used by the C3 / C4 bench."""
 import dataclasses
 
 import torch
+import torch.nn.functional as F
 
 import oracle
 from vf_b200 import dist as VD
@@ -38,7 +39,7 @@ def test_deberta_encoder_packing_invariance():
     cfg = dataclasses.replace(EN.DebertaConfig(), layers=2, hidden=128, heads=2, ffn=256, vocab=500,
                               position_buckets=16, max_relative_positions=64)
     _packing_invariance(EN.DebertaV3Encoder(cfg, device="cpu", dtype=torch.float32, attention_fn=_deb_attn,
-                                            add_norm=EN.add_layer_norm_torch), 500)
+                                            add_norm=EN.add_layer_norm_torch, act_fn=F.gelu), 500)
 
 
 def test_mt5_encoder_packing_invariance():
@@ -58,7 +59,7 @@ def test_deberta_position_scores_are_q_dot_kr():
         return _deb_attn(q, k, v, cu, ms, pk, pq, *rest)
 
     m = EN.DebertaV3Encoder(cfg, device="cpu", dtype=torch.float32, attention_fn=spy,
-                            add_norm=EN.add_layer_norm_torch)
+                            add_norm=EN.add_layer_norm_torch, act_fn=F.gelu)
     lengths, ids = EN.packed_batch(2, 5, 9, 100, seed=2)
     x, cu, lens = EN.select_sequences(lengths, ids, range(2))
     m.forward(x, cu, max(lens))

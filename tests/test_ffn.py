@@ -67,3 +67,10 @@ def test_gated_act_empty_is_a_no_op():
     lib = _lib.load()
     assert lib.vf_gated_act_fwd(ctypes.byref(_args(rows=0)), None) == _lib.VF_OK
     assert lib.vf_gated_act_fwd(None, None) == _lib.VF_EINVAL
+
+
+@pytest.mark.parametrize("act", [0, 1, 2, 3])
+def test_oracle_without_up_is_the_activation(act):
+    """up = None: the plain activation (the DeBERTa feed-forward uses the exact GELU)."""
+    g = torch.randn(64, 96, generator=torch.Generator().manual_seed(act)) * 3
+    torch.testing.assert_close(oracle.gated_act_ref(g, None, act), FALLBACK[act](g), rtol=2e-6, atol=1e-5)

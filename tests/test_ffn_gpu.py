@@ -5,6 +5,7 @@ import pytest
 import torch
 
 import oracle
+import vf_b200.ops  # noqa: F401  (registers torch.ops.vf_b200)
 
 pytestmark = pytest.mark.gpu
 
@@ -58,3 +59,23 @@ def test_mt5_c4_shape_and_empty():
     _check(gate, torch.randn(4096, 2816).to(torch.bfloat16), 0, "mT5 shape")
     e = torch.empty(0, 2816, dtype=torch.bfloat16, device="cuda")
     assert _op()(e, e).shape == (0, 2816)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("act", [0, 1, 2, 3])
+def test_activation_without_up(dtype, act):
+    """torch.ops.vf_b200.gated_act(x, None, act): out = act(x) (vector and scalar kernels)."""
+    for shape in ((1024, 4096), (37, 101)):
+        x = (torch.randn(*shape, generator=torch.Generator().manual_seed(act)) * 3).to(dtype)
+        out = torch.ops.vf_b200.gated_act(x.cuda(), None, act)
+        torch.cuda.synchronize()
+        ref = oracle.gated_act_ref(x, None, act)
+        torch.testing.assert_close(out.cpu().float(), ref.float(), **TOL[dtype], msg=f"{dtype} act {act} {shape}")
+
+
+def test_exact_gelu_matches_torch_gelu():
+    """The DeBERTa stack's activation against torch's own exact GELU on the GPU."""
+    import torch.nn.functional as F
+    from vf_b200.encoders import exact_gelu_kernel
+    x = (torch.randn(4096, 4096, generator=torch.Generator().manual_seed(5)) * 2).to(torch.bfloat16).cuda()
+    torch.testing.assert_close(exact_gelu_kernel(x).float(), F.gelu(x).float(), **TOL[torch.bfloat16])

@@ -24,6 +24,8 @@ def test_meta_shapes_and_dtypes(dtype):
     g = torch.empty(5, 7, 2816, **m)
     o = OPS.gated_act(g, g, 0)
     assert o.shape == g.shape and o.dtype == dtype
+    o = OPS.gated_act(g, None, 1)
+    assert o.shape == g.shape and o.dtype == dtype
     h = torch.empty(5, 7, 1024, **m)
     w = torch.empty(1024, **m)
     o = OPS.add_layer_norm(h, h, w, w, 1e-7)

@@ -1,4 +1,5 @@
-// sm_100a gated activation of the mT5 feed-forward: out = act(gate) * up.
+// sm_100a gated activation of the mT5 feed-forward: out = act(gate) * up; with up = NULL
+// the plain activation out = act(gate) (the DeBERTa feed-forward's exact GELU).
 //
 // Replaces the Triton kernel behind kernels/ff_fused.py:86 `fused_gelu_mul_dropout`
 // (_fused_gelu_mul_dropout_kernel, :23-74) on its inference path: activation in fp32
@@ -76,7 +77,7 @@ struct GatedView {
 
 // 16-byte vectors: kV elements of T.  Requires cols % kV == 0, 16-byte aligned bases and
 // row strides (checked on the host).  The activation is a template parameter.
-template <typename T, int kAct>
+template <typename T, int kAct, bool kGated>
 __global__ void gated_act_vec_kernel(const GatedView v) {
   constexpr int kV = 16 / sizeof(T);
   const long long vpr = v.cols / kV;                 // vectors per row
@@ -95,13 +96,16 @@ __global__ void gated_act_vec_kernel(const GatedView v) {
     if (cv >= vpr) { cv -= vpr; ++r; if (r >= v.rows) break; }
     const long long c = cv * kV;
     const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(gate + r * v.gs + c));
-    const uint4 u4 = __ldg(reinterpret_cast<const uint4*>(up + r * v.us + c));
+    const uint4 u4 = kGated ? __ldg(reinterpret_cast<const uint4*>(up + r * v.us + c)) : make_uint4(0, 0, 0, 0);
     const T* g = reinterpret_cast<const T*>(&g4);
     const T* u = reinterpret_cast<const T*>(&u4);
     uint4 o4;
     T* o = reinterpret_cast<T*>(&o4);
 #pragma unroll
-    for (int j = 0; j < kV; ++j) o[j] = Elem<T>::from(act_f(Elem<T>::f(g[j]), kAct) * Elem<T>::f(u[j]));
+    for (int j = 0; j < kV; ++j) {
+      const float a = act_f(Elem<T>::f(g[j]), kAct);
+      o[j] = Elem<T>::from(kGated ? a * Elem<T>::f(u[j]) : a);
+    }
     *reinterpret_cast<uint4*>(out + r * v.os + c) = o4;
   }
 }
@@ -114,7 +118,8 @@ __global__ void gated_act_scalar_kernel(const GatedView v) {
   T* out = static_cast<T*>(v.out);
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
     const long long r = i / v.cols, c = i - r * v.cols;
-    out[r * v.os + c] = Elem<T>::from(act_f(Elem<T>::ldg(gate + r * v.gs + c), v.act) * Elem<T>::ldg(up + r * v.us + c));
+    const float a = act_f(Elem<T>::ldg(gate + r * v.gs + c), v.act);
+    out[r * v.os + c] = Elem<T>::from(up != nullptr ? a * Elem<T>::ldg(up + r * v.us + c) : a);
   }
 }
 
@@ -123,6 +128,16 @@ int set_last_error(int code, const std::string& msg);   // vf_attention.cu: feed
 namespace {
 
 int ffn_fail(int code, const std::string& msg) { return set_last_error(code, msg); }
+
+template <typename T, bool kGated>
+void launch_vec(const GatedView& v, unsigned nb, int threads, cudaStream_t s) {
+  switch (v.act) {
+    case VF_ACT_GELU_TANH: gated_act_vec_kernel<T, VF_ACT_GELU_TANH, kGated><<<nb, threads, 0, s>>>(v); break;
+    case VF_ACT_GELU_ERF: gated_act_vec_kernel<T, VF_ACT_GELU_ERF, kGated><<<nb, threads, 0, s>>>(v); break;
+    case VF_ACT_RELU: gated_act_vec_kernel<T, VF_ACT_RELU, kGated><<<nb, threads, 0, s>>>(v); break;
+    default: gated_act_vec_kernel<T, VF_ACT_SILU, kGated><<<nb, threads, 0, s>>>(v); break;
+  }
+}
 
 template <typename T>
 int launch_gated(const GatedView& v, cudaStream_t s) {
@@ -133,20 +148,17 @@ int launch_gated(const GatedView& v, cudaStream_t s) {
   constexpr int kV = 16 / sizeof(T);
   const int es = sizeof(T);
   const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  const bool vec = v.cols % kV == 0 && al16(v.gate) && al16(v.up) && al16(v.out) && (v.gs * es) % 16 == 0 &&
-                   (v.us * es) % 16 == 0 && (v.os * es) % 16 == 0;
+  const bool gated = v.up != nullptr;
+  const bool vec = v.cols % kV == 0 && al16(v.gate) && (!gated || al16(v.up)) && al16(v.out) &&
+                   (v.gs * es) % 16 == 0 && (!gated || (v.us * es) % 16 == 0) && (v.os * es) % 16 == 0;
   const long long work = vec ? v.rows * (v.cols / kV) : v.rows * v.cols;
   const int threads = 256;
   // Enough resident blocks to cover the SMs several times; the kernels stride beyond.
   const long long blocks = std::max<long long>(1, std::min<long long>((work + threads - 1) / threads, 8LL * sm_count));
   const unsigned nb = static_cast<unsigned>(blocks);
   if (vec) {
-    switch (v.act) {
-      case VF_ACT_GELU_TANH: gated_act_vec_kernel<T, VF_ACT_GELU_TANH><<<nb, threads, 0, s>>>(v); break;
-      case VF_ACT_GELU_ERF: gated_act_vec_kernel<T, VF_ACT_GELU_ERF><<<nb, threads, 0, s>>>(v); break;
-      case VF_ACT_RELU: gated_act_vec_kernel<T, VF_ACT_RELU><<<nb, threads, 0, s>>>(v); break;
-      default: gated_act_vec_kernel<T, VF_ACT_SILU><<<nb, threads, 0, s>>>(v); break;
-    }
+    if (gated) launch_vec<T, true>(v, nb, threads, s);
+    else launch_vec<T, false>(v, nb, threads, s);
   } else
     gated_act_scalar_kernel<T><<<static_cast<unsigned>(blocks), threads, 0, s>>>(v);
   const cudaError_t e = cudaGetLastError();
@@ -165,8 +177,8 @@ int vf_gated_act_fwd(const vf_gated_act_args_t* a, void* stream) {
   if (a->act < VF_ACT_GELU_TANH || a->act > VF_ACT_SILU) return ffn_fail(VF_EINVAL, "gated act: unknown activation");
   if (a->rows < 0 || a->cols < 0) return ffn_fail(VF_EINVAL, "gated act: negative sizes");
   if (a->rows == 0 || a->cols == 0) return VF_OK;
-  if (!a->gate || !a->up || !a->out) return ffn_fail(VF_EINVAL, "gated act: gate, up and out must be non-null");
-  if (a->gate_row_stride < a->cols || a->up_row_stride < a->cols || a->out_row_stride < a->cols)
+  if (!a->gate || !a->out) return ffn_fail(VF_EINVAL, "gated act: gate and out must be non-null");
+  if (a->gate_row_stride < a->cols || (a->up != nullptr && a->up_row_stride < a->cols) || a->out_row_stride < a->cols)
     return ffn_fail(VF_EINVAL, "gated act: row strides must be at least cols (rows must not overlap)");
   vf::GatedView v{a->gate, a->up, a->out, a->rows, a->cols, a->gate_row_stride, a->up_row_stride, a->out_row_stride,
                   a->act};

@@ -327,35 +327,41 @@ at::Tensor as_rows(const at::Tensor& t, int64_t rows, int64_t cols) {
   return x;
 }
 
-at::Tensor gated_act(const at::Tensor& gate_in, const at::Tensor& up_in, int64_t act) {
+at::Tensor gated_act(const at::Tensor& gate_in, const std::optional<at::Tensor>& up_opt, int64_t act) {
   require_cuda(gate_in, "gate");
-  require_cuda(up_in, "up");
-  TORCH_CHECK(gate_in.sizes() == up_in.sizes(), "vf_b200: gate and up must have identical shapes");
-  TORCH_CHECK(gate_in.scalar_type() == up_in.scalar_type(), "vf_b200: gate and up must share a dtype");
+  const bool gated = up_opt.has_value() && up_opt->defined();
+  if (gated) {
+    require_cuda(*up_opt, "up");
+    TORCH_CHECK(gate_in.sizes() == up_opt->sizes(), "vf_b200: gate and up must have identical shapes");
+    TORCH_CHECK(gate_in.scalar_type() == up_opt->scalar_type(), "vf_b200: gate and up must share a dtype");
+  }
   TORCH_CHECK(gate_in.dim() >= 1, "vf_b200: gate must have at least one dimension");
   c10::cuda::CUDAGuard guard(gate_in.device());
   const int64_t cols = gate_in.size(-1);
   const int64_t rows = cols == 0 ? 0 : gate_in.numel() / cols;
-  const at::Tensor g = as_rows(gate_in, rows, cols), u = as_rows(up_in, rows, cols);
   at::Tensor out = at::empty(gate_in.sizes(), gate_in.options());
   if (rows == 0 || cols == 0) return out;
+  const at::Tensor g = as_rows(gate_in, rows, cols);
+  const at::Tensor u = gated ? as_rows(*up_opt, rows, cols) : at::Tensor();
   vf_gated_act_args_t a{};
   a.dtype = dtype_code(g);
   a.gate = g.data_ptr();
-  a.up = u.data_ptr();
+  a.up = gated ? u.data_ptr() : nullptr;
   a.out = out.data_ptr();
   a.rows = rows;
   a.cols = cols;
   a.gate_row_stride = rows > 1 ? g.stride(0) : cols;
-  a.up_row_stride = rows > 1 ? u.stride(0) : cols;
+  a.up_row_stride = gated ? (rows > 1 ? u.stride(0) : cols) : cols;
   a.out_row_stride = cols;
   a.act = static_cast<int32_t>(act);
   check_rc(vf_gated_act_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
   return out;
 }
 
-at::Tensor gated_act_meta(const at::Tensor& gate, const at::Tensor&, int64_t) { return at::empty_like(gate); }
-at::Tensor gated_act_cpu(const at::Tensor&, const at::Tensor&, int64_t) {
+at::Tensor gated_act_meta(const at::Tensor& gate, const std::optional<at::Tensor>&, int64_t) {
+  return at::empty_like(gate);
+}
+at::Tensor gated_act_cpu(const at::Tensor&, const std::optional<at::Tensor>&, int64_t) {
   TORCH_CHECK(false, "vf_b200: gate and up must be CUDA tensors (no CPU implementation)");
 }
 
@@ -464,7 +470,7 @@ TORCH_LIBRARY(vf_b200, m) {
   m.def("deberta_attention(Tensor q, Tensor k, Tensor v, Tensor? seq_lengths, Tensor? pos_key, "
         "Tensor? pos_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "
         "bool use_log_bucket) -> Tensor");
-  m.def("gated_act(Tensor gate, Tensor up, int act) -> Tensor");
+  m.def("gated_act(Tensor gate, Tensor? up, int act) -> Tensor");
   m.def("add_layer_norm(Tensor x, Tensor residual, Tensor weight, Tensor? bias, float eps) -> Tensor");
   m.def("deberta_attention_varlen(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, int max_seqlen, Tensor? pos_key, "
         "Tensor? pos_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "

@@ -8,8 +8,8 @@ stacks measure encoder tokens/s with the hot path in place:
   DebertaV3Encoder  models/deberta_v2/deberta_v2_encoder.py (DebertaV2 embeddings without
                     absolute positions, DisentangledSelfAttentionV2._flash_forward :246-328
                     with share_att_key, c2p|p2c, position_buckets 256 / max_relative 512,
-                    rel_embeddings + LayerNorm, GELU FFN, post-LayerNorm residuals through
-                    this package's fused_add_layer_norm as at :507 / :566).
+                    rel_embeddings + LayerNorm, exact-GELU FFN, post-LayerNorm residuals
+                    through this package's fused_add_layer_norm as at :507 / :566).
   MT5Encoder        models/mt5/mt5_encoder.py (T5 RMS LayerNorm, no QK scaling, the bias
                     table of layer 0 shared by all layers :546-566, gated-GELU FFN with the
                     tanh GELU through this package's fused_gelu_mul_dropout as at :418,
@@ -70,6 +70,14 @@ def add_layer_norm_torch(x: torch.Tensor, residual: torch.Tensor, w: torch.Tenso
     return _layer_norm(x + residual, w, b, eps)
 
 
+def exact_gelu_kernel(x: torch.Tensor) -> torch.Tensor:
+    """The DeBERTa feed-forward's exact (erf) GELU on this package's activation kernel
+    (torch.ops.vf_b200.gated_act with no `up`): one pass at the HBM rate."""
+    import vf_b200.ops  # noqa: F401
+    from vf_b200 import _lib
+    return torch.ops.vf_b200.gated_act(x, None, _lib.VF_ACT_GELU_ERF)
+
+
 def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     # T5LayerNorm (no mean subtraction, no bias) as torch's fused RMS norm, which keeps the
     # variance in fp32 for 16-bit inputs like models/mt5/mt5_encoder.py does
@@ -82,7 +90,7 @@ class DebertaV3Encoder:
     any function of the same signature, e.g. a CPU oracle)."""
 
     def __init__(self, cfg: DebertaConfig = DebertaConfig(), device="cuda", dtype=torch.bfloat16, seed: int = 0,
-                 attention_fn=None, add_norm=None):
+                 attention_fn=None, add_norm=None, act_fn=None):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         g = torch.Generator(device=self.device).manual_seed(seed)
         E, F_, S2 = cfg.hidden, cfg.ffn, 2 * cfg.position_buckets
@@ -107,6 +115,9 @@ class DebertaV3Encoder:
         if add_norm is None:
             from kernels.fused_add_layernorm import fused_add_layer_norm as add_norm
         self.add_norm = add_norm
+        # torch's exact GELU (the reference's ACT2FN["gelu"]); exact_gelu_kernel, this
+        # package's activation-only kernel, measured the same C3 tokens/s in its place
+        self.act_fn = F.gelu if act_fn is None else act_fn
 
     @torch.no_grad()
     def forward(self, ids: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
@@ -127,7 +138,7 @@ class DebertaV3Encoder:
                                     cfg.position_buckets, cfg.max_relative_positions, True)
             a = torch.addmm(L["bo"], ctx.reshape(T, E).to(h.dtype), L["wo"].t())
             h = self.add_norm(a, h, *L["ln1"], cfg.eps)
-            f = F.gelu(torch.addmm(L["b1"], h, L["w1"].t()))
+            f = self.act_fn(torch.addmm(L["b1"], h, L["w1"].t()))
             h = self.add_norm(torch.addmm(L["b2"], f, L["w2"].t()), h, *L["ln2"], cfg.eps)
         return h
 

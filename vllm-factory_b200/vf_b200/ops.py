@@ -15,7 +15,7 @@ strides and the current CUDA stream and calls the C ABI of libvf_b200.so:
                                              pos_query?, causal, sm_scale?, position_buckets,
                                              max_relative_distance, use_log_bucket)   # packed
 
-  torch.ops.vf_b200.gated_act(gate, up, act)                  # mT5 FFN: act(gate) * up
+  torch.ops.vf_b200.gated_act(gate, up, act)                  # mT5 FFN: act(gate) * up (up=None: act(gate))
   torch.ops.vf_b200.add_layer_norm(x, residual, w, b, eps)   # DeBERTa: LayerNorm(x + residual)
 
 All borrow their inputs (layouts TMA cannot describe are copied contiguous), allocate
