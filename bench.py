@@ -1,31 +1,36 @@
 """Benchmark of the relative-position attention hot path (one JSON line on rank 0).
 
-Default workload (the metric's own configuration): one mT5-large
-encoder self-attention layer with the T5 relative-position bias, bf16, 16 sequences x 768
-positions (valid lengths ~ U[256, 768], right padding), 16 heads x 64.  A "step" is one
-call of the drop-in `kernels.flash_attention_rpb.flash_attention_rpb_final` on that batch.
+Default run: the headline is one mT5-large encoder self-attention layer with the T5
+relative-position bias, bf16, 16 sequences x 768 positions (valid lengths ~ U[256, 768],
+right padding), 16 heads x 64.  A "step" is one call of the drop-in
+`kernels.flash_attention_rpb.flash_attention_rpb_final` on that batch.  The same run adds
+two sub-results with the same keys: the DeBERTa-v3-large disentangled attention layer
+(8 x 512, U[64, 512]; the fused mode, whose position contractions run inside the kernel,
+when the build has it) and the 24-layer DeBERTa-v3-large encoder stack over 256 packed
+sequences (encoder tokens/s).
 
-  value        attention TFLOP/s over the whole job (valid work: 4*H*D*sum L_i^2), inputs
-               resident in HBM; each step reads a different input set (the rotation
+  value        attention TFLOP/s over the whole job (valid work: 4*H*D*sum L_i^2, plus the
+               position contractions 4*H*D*sum L_i*P(L_i) where the kernel does them),
+               inputs resident in HBM; each step reads a different input set (the rotation
                spans > 3x the 126 MB L2), so no step is served from L2.
   e2e          the same metric through the same public call with pinned HOST buffers:
-               every step copies q, k, v, table and mask host->device and the output
-               device->host inside the timed region; copies of neighbouring steps overlap
-               the compute (upload, compute and download streams, two device slots).
+               every step copies the inputs host->device and the output device->host
+               inside the timed region; copies of neighbouring steps overlap the compute
+               (upload, compute and download streams, two device slots).
   roofline     dominant kernel vs the measured dense bf16 peak (MEASURED_PEAKS.json).
   cpu_baseline the oracle (CPU restatement of the reference's torch path) on this host.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs its own 16-sequence shard
-(independent sequences, weak scaling); NCCL is used only for the barrier and to take the
-max time over ranks.  `--impl reference` times the reference's CPU implementation (the
-oracle port) on rank 0 and prints the same metric.
+Multi-GPU (torchrun, one process per GPU): for the attention lines every rank runs its own
+batch with the same valid lengths as rank 0's (weak scaling); the encoder stack splits one
+256-sequence batch over the ranks by LPT on estimated FLOPs (strong scaling).  NCCL carries
+only the barrier and the max-time / summed-work reductions.  `--impl reference` times the
+reference's CPU implementation (the oracle port) on rank 0 and prints the same metric with
+the same `config`.
 
-Other workloads (`--workload`): deberta_c1 / deberta_c1_fp32 / deberta_c5_<L> (DeBERTa
-attention), mt5_c2_varlen / deberta_c1_varlen (packed batches), and the encoder stacks
-deberta_c3 / mt5_c4: a 256-sequence packed batch partitioned by sequence over the ranks
-(LPT on estimated FLOPs, strong scaling), 24 layers per step, value = encoder tokens/s;
-mt5_ffn_act / deberta_add_ln: the HBM-bound ops beside the path (the mT5 gated-GELU, the
-DeBERTa residual add + LayerNorm), value = GB/s.
+Named workloads (`--workload`): mt5_c2, mt5_c2_varlen, deberta_c1[_fused], deberta_c1_fp32,
+deberta_c1_varlen[_fused], deberta_c5_<L>[_fused] (L = 1024, 2048, 4096), the encoder
+stacks deberta_c3 / mt5_c4, and the HBM-bound ops beside the path, mt5_ffn_act /
+deberta_add_ln (value = GB/s).
 """
 from __future__ import annotations
 
@@ -182,13 +187,60 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- workloads
+ATTN_WORKLOADS = ("mt5_c2", "mt5_c2_varlen", "deberta_c1", "deberta_c1_fp32", "deberta_c1_varlen",
+                  "deberta_c1_fused", "deberta_c1_varlen_fused", "deberta_c5_1024", "deberta_c5_2048",
+                  "deberta_c5_4096", "deberta_c5_1024_fused", "deberta_c5_2048_fused", "deberta_c5_4096_fused")
+COMPAT_NOTE = ("compat: the caller's pos_key = Q.Kr^T / pos_query = K.Qr^T products (cuBLAS) are inputs, "
+               "made outside the kernel; FLOPs count QK^T + PV only")
+FUSED_NOTE = ("fused: rel_key / rel_query in, Q.Kr^T and K.Qr^T on tcgen05 inside the kernel; "
+              "FLOPs count QK^T + PV + both position contractions at their distinct-index width")
+
+
+def attention_config(name: str) -> dict:
+    """The `config` object of an attention workload; both arms print the same one."""
+    if name.startswith("mt5_c2"):
+        cfg = {"workload": "mT5-large encoder self-attention layer, T5 RPB 32 buckets / max_distance 128",
+               "global_batch": 16, "seq_len": 768, "heads": 16, "head_dim": 64,
+               "lengths": "U[256,768] right-padded"}
+        if name == "mt5_c2_varlen":
+            cfg["workload"] += ", packed (cu_seqlens)"
+            cfg["lengths"] = "U[256,768] packed, no padding"
+        return cfg
+    if name.startswith("deberta_c1"):
+        cfg = {"workload": "DeBERTa-v3-large disentangled self-attention layer, c2p|p2c, 256 buckets / max_rel 512",
+               "global_batch": 8, "seq_len": 512, "heads": 16, "head_dim": 64, "lengths": "U[64,512] right-padded"}
+        if name == "deberta_c1_fp32":
+            cfg["workload"] += ", fp32 tensors in and out"
+        if "varlen" in name:
+            cfg["workload"] += ", packed (cu_seqlens)"
+            cfg["lengths"] = "U[64,512] packed, no padding"
+        cfg["mode"] = FUSED_NOTE if name.endswith("_fused") else COMPAT_NOTE
+        return cfg
+    if name.startswith("deberta_c5"):
+        L = int(name.split("_")[2])
+        return {"workload": f"DeBERTa long-context disentangled attention, seq {L}, full length",
+                "global_batch": 16384 // L, "seq_len": L, "heads": 16, "head_dim": 64,
+                "mode": FUSED_NOTE if name.endswith("_fused") else COMPAT_NOTE}
+    if name in ENCODER_NAMES:
+        from vf_b200 import encoders as EN
+        tokens = int(encoder_setup(name)[2].sum())
+        return {"workload": ENCODER_NAMES[name], "sequences": 256, "layers": 24, "tokens": tokens,
+                "lengths": "U[128,768]" if name == "deberta_c3" else "U[512,768]",
+                "partition": "packed batch, LPT by estimated FLOPs over ranks"}
+    raise SystemExit(f"unknown workload {name}")
+
+
 def build_workload(name: str, rank: int, device):
-    """Returns (list of input dicts, call(inputs) -> out, flops per step, tokens per step, config)."""
+    """Returns (list of input dicts, call(inputs) -> out, flops per step, tokens per step, config,
+    keys copied per step, lengths, launches per step).  Weak scaling: rank r's batch has the
+    valid lengths of rank 0's batch (rotated) and its own seeded values."""
     from vf_b200 import workloads as W
 
+    cfg = attention_config(name)
+    launches = 1
     if name == "mt5_c2":
         from kernels.flash_attention_rpb import flash_attention_rpb_final
-        base = W.mt5_attention_inputs(seed=1000 + rank, device=device)
+        base = W.mt5_attention_inputs(seed=1000 + rank, device=device, lengths=W.rank_lengths("mt5", rank))
         lens = base["lengths"].tolist()
         flops = W.core_flops(lens)
 
@@ -197,14 +249,10 @@ def build_workload(name: str, rank: int, device):
                                              x["padding_mask"], 0.0, 1.0)
 
         per_set = sum(base[k].numel() * base[k].element_size() for k in ("q", "k", "v")) * 4 // 3
-        cfg = {"workload": "C2 mT5-large encoder self-attention layer, T5 RPB 32 buckets/128",
-               "global_batch": 16, "seq_len": 768, "heads": 16, "head_dim": 64,
-               "lengths": "U[256,768] right-padded"}
         keys = ("q", "k", "v", "rpb_table", "padding_mask")
     elif name == "mt5_c2_varlen":
-        # C2's sequences packed back to back (cu_seqlens), no padding rows or mask.
         from kernels.flash_attention_rpb import flash_attention_rpb_varlen
-        base = W.mt5_varlen_inputs(seed=1000 + rank, device=device)
+        base = W.mt5_varlen_inputs(seed=1000 + rank, device=device, lengths=W.rank_lengths("mt5", rank))
         lens = base["lengths"].tolist()
         flops = W.core_flops(lens)
 
@@ -213,54 +261,59 @@ def build_workload(name: str, rank: int, device):
                                               x["rpb_table"], 32, 128, False, 1.0)
 
         per_set = sum(base[k].numel() * base[k].element_size() for k in ("q", "k", "v")) * 4 // 3
-        cfg = {"workload": "C2 mT5-large encoder self-attention layer, T5 RPB 32 buckets/128, packed (cu_seqlens)",
-               "global_batch": 16, "seq_len": 768, "heads": 16, "head_dim": 64,
-               "lengths": "U[256,768] packed, no padding"}
         keys = ("q", "k", "v", "rpb_table", "cu_seqlens")
-    elif name == "deberta_c1_varlen":
-        # C1's sequences packed back to back (cu_seqlens), position rows packed alike.
+    elif name.startswith("deberta_c1_varlen"):
         from kernels.flash_deberta_attention import flash_deberta_attention_varlen
-        base = W.deberta_varlen_inputs(seed=2000 + rank, device=device)
+        fused = name.endswith("_fused")
+        base = W.deberta_varlen_inputs(seed=2000 + rank, device=device, lengths=W.rank_lengths("deberta", rank))
         lens = base["lengths"].tolist()
-        flops = W.core_flops(lens) + W.deberta_pos_flops(lens)
+        flops = W.core_flops(lens) + (W.deberta_pos_flops(lens) if fused else 0.0)
+        if fused:
+            keys = ("q", "k", "v", "rel_key", "rel_query", "cu_seqlens")
+            launches = 2
 
-        def call(x):
-            return flash_deberta_attention_varlen(x["q"], x["k"], x["v"], x["cu_seqlens"], x["max_seqlen"],
-                                                  x["pos_key"], x["pos_query"], False, x["sm_scale"], 256, 512, True)
+            def call(x):
+                return flash_deberta_attention_varlen(x["q"], x["k"], x["v"], x["cu_seqlens"], x["max_seqlen"],
+                                                      None, None, False, x["sm_scale"], 256, 512, True,
+                                                      rel_key=x["rel_key"], rel_query=x["rel_query"])
+        else:
+            keys = ("q", "k", "v", "pos_key", "pos_query", "cu_seqlens")
 
-        per_set = sum(base[k].numel() * base[k].element_size() for k in ("q", "k", "v", "pos_key", "pos_query"))
-        cfg = {"workload": "C1 DeBERTa-v3-large disentangled layer (bf16 on GPU), c2p|p2c, 256 buckets, packed (cu_seqlens)",
-               "global_batch": 8, "seq_len": 512, "lengths": "U[64,512] packed, no padding", "heads": 16,
-               "head_dim": 64, "mode": "compat (precomputed pos_key/pos_query)"}
-        keys = ("q", "k", "v", "pos_key", "pos_query", "cu_seqlens")
+            def call(x):
+                return flash_deberta_attention_varlen(x["q"], x["k"], x["v"], x["cu_seqlens"], x["max_seqlen"],
+                                                      x["pos_key"], x["pos_query"], False, x["sm_scale"], 256, 512,
+                                                      True)
+        per_set = sum(base[k].numel() * base[k].element_size() for k in keys if k != "cu_seqlens")
     elif name.startswith("deberta_c1") or name.startswith("deberta_c5"):
         from kernels.flash_deberta_attention import flash_deberta_attention
-        if name == "deberta_c1":
-            base = W.deberta_attention_inputs(seed=2000 + rank, device=device)
-            cfg = {"workload": "C1 DeBERTa-v3-large disentangled layer (bf16 on GPU), c2p|p2c, 256 buckets",
-                   "global_batch": 8, "seq_len": 512, "lengths": "U[64,512] right-padded"}
-        elif name == "deberta_c1_fp32":
-            # BASELINE C1's own dtype: fp32 tensors in and out; the op computes with fp16
-            # operands (TF32's mantissa) and fp32 softmax / accumulation.
-            base = W.deberta_attention_inputs(seed=2000 + rank, device=device, dtype=torch.float32)
-            cfg = {"workload": "C1 DeBERTa-v3-large disentangled layer, fp32 inputs and output, c2p|p2c, 256 buckets",
-                   "global_batch": 8, "seq_len": 512, "lengths": "U[64,512] right-padded",
-                   "_dtype": "f32 in/out (fp16 operands, fp32 accumulate)"}
+        fused = name.endswith("_fused")
+        if name.startswith("deberta_c1"):
+            dt = torch.float32 if name == "deberta_c1_fp32" else torch.bfloat16
+            base = W.deberta_attention_inputs(seed=2000 + rank, device=device, dtype=dt,
+                                              lengths=W.rank_lengths("deberta", rank))
+            if dt == torch.float32:
+                cfg["_dtype"] = "f32"
         else:
-            L = int(name.split("_")[-1])
+            L = int(name.split("_")[2])
             base = W.deberta_attention_inputs(seed=3000 + rank, device=device, B=16384 // L, L=L,
                                               lengths=[L] * (16384 // L))
-            cfg = {"workload": f"C5 DeBERTa long-context sweep, seq {L}", "global_batch": 16384 // L, "seq_len": L}
         lens = base["lengths"].tolist()
-        flops = W.core_flops(lens) + W.deberta_pos_flops(lens)
+        flops = W.core_flops(lens) + (W.deberta_pos_flops(lens) if fused else 0.0)
+        if fused:
+            keys = ("q", "k", "v", "rel_key", "rel_query", "seq_lengths")
+            launches = 2
 
-        def call(x):
-            return flash_deberta_attention(x["q"], x["k"], x["v"], x["seq_lengths"], x["pos_key"], x["pos_query"],
-                                           False, x["sm_scale"], 256, 512, True)
+            def call(x):
+                return flash_deberta_attention(x["q"], x["k"], x["v"], x["seq_lengths"], None, None, False,
+                                               x["sm_scale"], 256, 512, True, rel_key=x["rel_key"],
+                                               rel_query=x["rel_query"])
+        else:
+            keys = ("q", "k", "v", "pos_key", "pos_query", "seq_lengths")
 
-        per_set = sum(base[k].numel() * base[k].element_size() for k in ("q", "k", "v", "pos_key", "pos_query"))
-        keys = ("q", "k", "v", "pos_key", "pos_query", "seq_lengths")
-        cfg.update({"heads": 16, "head_dim": 64, "mode": "compat (precomputed pos_key/pos_query)"})
+            def call(x):
+                return flash_deberta_attention(x["q"], x["k"], x["v"], x["seq_lengths"], x["pos_key"],
+                                               x["pos_query"], False, x["sm_scale"], 256, 512, True)
+        per_set = sum(base[k].numel() * base[k].element_size() for k in keys if k != "seq_lengths")
     else:
         raise SystemExit(f"unknown workload {name}")
 
@@ -269,8 +322,8 @@ def build_workload(name: str, rank: int, device):
     for _ in range(n_sets - 1):
         sets.append({k: (v.clone() if isinstance(v, torch.Tensor) and v.is_cuda and k in keys else v)
                      for k, v in base.items()})
-    cfg["l2"] = f"{n_sets} rotating input sets ({per_set / 2**20:.0f} MiB each) > 3x L2; no flush"
-    return sets, call, flops, float(sum(lens)), cfg, keys, lens
+    cfg["_l2"] = f"{n_sets} rotating input sets ({per_set / 2**20:.0f} MiB each) > 3x L2; no flush"
+    return sets, call, flops, float(sum(lens)), cfg, keys, lens, launches
 
 
 def cpu_baseline(name: str, lens, budget_s: float = 12.0):
@@ -295,26 +348,38 @@ def cpu_baseline(name: str, lens, budget_s: float = 12.0):
         dt = time.perf_counter() - t0
         sample = f"{n} sequences of the C2 batch, one at a time, fp32 torch on CPU (oracle port of the reference's SDPA path)"
     else:
+        # Compat lines: the op's own work (pos_key / pos_query are inputs), core FLOPs only.
+        # Fused lines: the position products Q.Kr^T and K.Qr^T run inside the timed loop too
+        # (as the reference's caller does them), core + position FLOPs.
+        fused = name.endswith("_fused")
         x = W.deberta_attention_inputs(seed=2000, device="cpu")
         flops_done, t0, n = 0.0, time.perf_counter(), 0
         while True:
             b = n % x["q"].shape[0]
             sl = slice(b, b + 1)
-            oracle.deberta_attention_ref(x["q"][sl].float(), x["k"][sl].float(), x["v"][sl].float(),
-                                         x["seq_lengths"][sl], x["pos_key"][sl].float(), x["pos_query"][sl].float(),
+            q, k = x["q"][sl].float(), x["k"][sl].float()
+            if fused:
+                pk = torch.matmul(q, x["rel_key"].float().transpose(-1, -2))
+                pq = torch.matmul(k, x["rel_query"].float().transpose(-1, -2))
+            else:
+                pk, pq = x["pos_key"][sl].float(), x["pos_query"][sl].float()
+            oracle.deberta_attention_ref(q, k, x["v"][sl].float(), x["seq_lengths"][sl], pk, pq,
                                          False, x["sm_scale"], 256, 512, True, dtype=torch.float32)
             L = int(x["lengths"][b])
-            flops_done += W.core_flops([L]) + W.deberta_pos_flops([L])
+            flops_done += W.core_flops([L]) + (W.deberta_pos_flops([L]) if fused else 0.0)
             n += 1
             if time.perf_counter() - t0 > budget_s:
                 break
         dt = time.perf_counter() - t0
-        sample = f"{n} sequences of the C1 batch, fp32 torch on CPU (oracle port of the reference's op fallback)"
+        sample = (f"{n} sequences of the C1 batch, fp32 torch on CPU (oracle port of the reference's op fallback"
+                  + (", with the caller's two position products)" if fused else ")"))
     return {"value": flops_done / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
 
 
 # ----------------------------------------------------------------------------- encoder stacks
 ENCODER_WORKLOADS = ("deberta_c3", "mt5_c4")
+ENCODER_NAMES = {"deberta_c3": "DeBERTa-v3-large 24-layer encoder stack, 256 packed sequences",
+                 "mt5_c4": "mT5-large 24-layer encoder stack, 256 packed sequences"}
 
 
 def encoder_setup(name: str):
@@ -362,13 +427,14 @@ def encoder_cpu_baseline(name: str, budget_s: float = 15.0):
             "kind": "port", "sample": f"first {n} sequences, 2 layers, fp32 torch on CPU with the oracle's attention"}
 
 
-def run_encoder(args, world: int, rank: int, dev, warmup: int):
+def run_encoder(args, name: str, steps: int, world: int, rank: int, dev, warmup: int, cpu_base: bool):
     """C3 / C4: the 256-sequence packed batch is partitioned by sequence over the ranks
     (LPT on estimated FLOPs), each rank runs the 24-layer stack on its shard; value =
-    encoder tokens/s of the whole job (total valid tokens / max rank time)."""
+    encoder tokens/s of the whole job (total valid tokens / max rank time).  Every rank
+    takes the same collective steps; rank 0 gets the line, the others None."""
     from vf_b200 import dist as VD
     from vf_b200 import encoders as EN
-    cls, cfg, lengths, ids, attn = encoder_setup(args.workload)
+    cls, cfg, lengths, ids, attn = encoder_setup(name)
     model = cls(cfg, device=dev, seed=0)
     gemm_tok = model.flops_per_token_gemm()
     costs = [gemm_tok * int(L) + cfg.layers * attn(int(L)) for L in lengths.tolist()]
@@ -392,7 +458,7 @@ def run_encoder(args, world: int, rank: int, dev, warmup: int):
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         model.forward(x_dev, cu_dev, max_len)
     ev1.record(stream)
     torch.cuda.synchronize()
@@ -400,12 +466,12 @@ def run_encoder(args, world: int, rank: int, dev, warmup: int):
     clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1)
     ms_max, flops_all, tokens_all = VD.reduce_timing(ms, flops, tokens, dev)
-    value = tokens_all * args.steps / (ms_max * 1e-3)
+    value = tokens_all * steps / (ms_max * 1e-3)
 
     e2e = None
     if not args.no_e2e:
         host = {"ids": x_ids.pin_memory(), "cu": cu.pin_memory()}
-        n_e2e = max(3, min(args.steps, 10))
+        n_e2e = max(3, min(steps, 10))
         ems, h2d, d2h = pipelined_e2e(dev, host, lambda x: model.forward(x["ids"], x["cu"], max_len), n_e2e, world)
         barrier()
         e2e = {"value": tokens_all * n_e2e / (ems * 1e-3), "unit": "tokens/s", "pipelined": True,
@@ -413,24 +479,21 @@ def run_encoder(args, world: int, rank: int, dev, warmup: int):
     if rank != 0:
         return None
     peaks = measured_peaks()
-    achieved = flops / (ms / args.steps * 1e-3) / 1e12
-    name = {"deberta_c3": "C3 DeBERTa-v3-large 24-layer encoder stack", "mt5_c4": "C4 mT5-large 24-layer encoder stack"}
-    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": name[args.workload], "sequences": int(len(lengths)),
-                       "tokens": int(lengths.sum()), "layers": cfg.layers,
-                       "lengths": "U[128,768]" if args.workload == "deberta_c3" else "U[512,768]",
-                       "partition": "packed batch, LPT by estimated FLOPs over ranks",
-                       "l2": "weights (>0.8 GB) and activations exceed L2; no flush"},
+    achieved = flops / (ms / steps * 1e-3) / 1e12
+    cfg_line = attention_config(name)
+    cfg_line["tokens"] = int(lengths.sum())
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg_line,
+            "l2": "weights (>0.8 GB) and activations exceed L2; no flush",
             "attention_flops_share": sum(cfg.layers * attn(int(lengths[i])) for i in mine) / flops,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
-                         "frac": achieved / peaks["bf16"], "traffic": None,
-                         "peak_source": f"{peaks['source']} bf16 dense (burst)",
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_sustained"], "unit": "TFLOP/s",
+                         "frac": achieved / peaks["bf16_sustained"], "traffic": None,
+                         "peak_source": f"{peaks['source']} bf16 dense (sustained: a 24-layer step runs for seconds)",
                          "what": "whole stack: GEMM + attention algorithmic FLOPs of rank 0's shard per second"},
-            "gpu_launches": args.steps * cfg.layers, "clocks": clocks, "e2e": e2e}
-    if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = encoder_cpu_baseline(args.workload)
+            "gpu_launches": steps * cfg.layers * model.own_launches_per_layer(), "clocks": clocks, "e2e": e2e}
+    if world == 1 and cpu_base:
+        line["cpu_baseline"] = encoder_cpu_baseline(name)
     return line
 
 
@@ -552,65 +615,12 @@ def run_add_layer_norm(args, world: int, rank: int, dev, warmup: int):
     return _run_hbm_op(args, world, rank, dev, warmup, sets, call, 3 * T * E * 2, cfg, add_layer_norm_cpu_baseline)
 
 
-# ----------------------------------------------------------------------------- main
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="mt5_c2")
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-e2e", action="store_true")
-    args = ap.parse_args()
-    warmup = max(args.warmup, 3)
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-
-    if args.impl == "reference":
-        if rank != 0:
-            return
-        if args.workload in ENCODER_WORKLOADS:
-            cb = encoder_cpu_baseline(args.workload)
-        elif args.workload == "mt5_ffn_act":
-            cb = gated_act_cpu_baseline()
-        elif args.workload == "deberta_add_ln":
-            cb = add_layer_norm_cpu_baseline()
-        else:
-            cb = cpu_baseline(args.workload, None, budget_s=max(5.0, min(60.0, 2.0 * args.steps)))
-        line = {"metric": METRIC, "value": cb["value"], "unit": cb["unit"], "n_gpus": args.gpus, "steps": args.steps,
-                "warmup": warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                "dtype": "f32", "data": "synthetic", "impl": "reference",
-                "config": {"workload": args.workload},
-                "cpu_baseline": cb,
-                "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line))
-        return
-
-    if not torch.cuda.is_available():
-        raise SystemExit("bench.py needs a CUDA GPU")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        os.environ["NCCL_DEBUG"] = "WARN"   # rank 0's stdout carries only the JSON line
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=dev)
-    import vf_b200
-    vf_b200.load()
-
-    if args.workload in ENCODER_WORKLOADS or args.workload in ("mt5_ffn_act", "deberta_add_ln"):
-        runner = {"mt5_ffn_act": run_gated_act, "deberta_add_ln": run_add_layer_norm}.get(args.workload, run_encoder)
-        line = runner(args, world, rank, dev, warmup)
-        if line is not None:
-            print(json.dumps(line))
-        if world > 1:
-            torch.distributed.destroy_process_group()
-        return
-
-    sets, call, flops, tokens, cfg, keys, lens = build_workload(args.workload, rank, dev)
+# ----------------------------------------------------------------------------- attention lines
+def run_attention(args, name: str, steps: int, world: int, rank: int, dev, warmup: int, cpu_base: bool):
+    """One attention workload: `steps` calls of the drop-in, each on a different input set,
+    timed on the device; value = valid FLOPs of all ranks / max rank time.  Every rank takes
+    the same collective steps; rank 0 gets the line, the others None."""
+    sets, call, flops, tokens, cfg, keys, lens, launches = build_workload(name, rank, dev)
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -621,14 +631,14 @@ def main():
         call(sets[i % len(sets)])
     torch.cuda.synchronize()
 
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(dev.index or 0)
     sampler.start()
     barrier()
     torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for i in range(args.steps):
+    for i in range(steps):
         call(sets[i % len(sets)])
     ev1.record(stream)
     torch.cuda.synchronize()
@@ -636,54 +646,140 @@ def main():
     clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1)
 
-    t = torch.tensor([ms, flops, tokens], dtype=torch.float64, device=dev)
-    if world > 1:
-        tmax = t[:1].clone()
-        torch.distributed.all_reduce(tmax, op=torch.distributed.ReduceOp.MAX)
-        tsum = t[1:].clone()
-        torch.distributed.all_reduce(tsum, op=torch.distributed.ReduceOp.SUM)
-        ms_max, flops_all, tokens_all = tmax.item(), tsum[0].item(), tsum[1].item()
-    else:
-        ms_max, flops_all, tokens_all = ms, flops, tokens
-    value = flops_all * args.steps / (ms_max * 1e-3) / 1e12
-    ms_step = ms_max / args.steps
+    from vf_b200 import dist as VD
+    ms_max, flops_all, tokens_all = VD.reduce_timing(ms, flops, tokens, dev)
+    value = flops_all * steps / (ms_max * 1e-3) / 1e12
 
     # ---- end to end through the public call, host buffers, copies inside the timed region
     e2e = None
     if not args.no_e2e:
         host = {k: (v.cpu().pin_memory() if isinstance(v, torch.Tensor) and v.is_cuda and k in keys else v)
                 for k, v in sets[0].items()}
-        n_e2e = max(3, min(args.steps, 30))
+        n_e2e = max(3, min(steps, 30))
         ems, h2d, d2h = pipelined_e2e(dev, {k: v for k, v in host.items() if k in keys},
                                       lambda x: call({**host, **x}), n_e2e, world)
         barrier()
         e2e = {"value": flops_all * n_e2e / (ems * 1e-3) / 1e12, "unit": "TFLOP/s", "pipelined": True,
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": n_e2e}
-
-    if world > 1:
-        torch.distributed.barrier()
+    barrier()
     if rank != 0:
-        if world > 1:
-            torch.distributed.destroy_process_group()
-        return
+        return None
 
     peaks = measured_peaks()
     dtype_label = cfg.pop("_dtype", "bf16")
-    achieved = flops / (ms / args.steps * 1e-3) / 1e12      # this rank's launches
+    l2_note = cfg.pop("_l2")
+    achieved = flops / (ms / steps * 1e-3) / 1e12      # this rank's launches
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
-                "frac": achieved / peaks["bf16"], "traffic": committed_traffic(args.workload),
+                "frac": achieved / peaks["bf16"], "traffic": committed_traffic(name),
                 "peak_source": f"{peaks['source']} bf16 dense (burst)",
                 "algorithmic_flops_per_launch": flops}
-    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": dtype_label, "data": "synthetic", "config": cfg,
-            "tokens_per_s": tokens_all * args.steps / (ms_max * 1e-3),
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms_max / steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": dtype_label, "data": "synthetic", "config": cfg, "l2": l2_note,
+            "tokens_per_s": tokens_all * steps / (ms_max * 1e-3),
             "pct_bf16_peak": value / (peaks["bf16"] * world),
-            "roofline": roofline, "gpu_launches": args.steps, "clocks": clocks, "e2e": e2e}
-    if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.workload, lens)
-    print(json.dumps(line))
+            "roofline": roofline, "gpu_launches": steps * launches, "clocks": clocks, "e2e": e2e}
+    if world == 1 and cpu_base:
+        line["cpu_baseline"] = cpu_baseline(name, lens)
+    return line
+
+
+def deberta_line_workload() -> str:
+    """The DeBERTa attention sub-result: the fused mode when this build has it."""
+    from kernels import flash_deberta_attention as FD
+    return "deberta_c1_fused" if getattr(FD, "HAS_FUSED_POSITIONS", False) else "deberta_c1"
+
+
+# ----------------------------------------------------------------------------- reference arm
+def reference_line(args, name: str) -> dict:
+    if name in ENCODER_WORKLOADS:
+        cb = encoder_cpu_baseline(name)
+        cfg = attention_config(name)
+    elif name == "mt5_ffn_act":
+        cb, cfg = gated_act_cpu_baseline(), {"workload": name}
+    elif name == "deberta_add_ln":
+        cb, cfg = add_layer_norm_cpu_baseline(), {"workload": name}
+    else:
+        cb = cpu_baseline(name, None, budget_s=max(5.0, min(60.0, 2.0 * args.steps)))
+        cfg = attention_config(name)
+    return {"metric": METRIC, "value": cb["value"], "unit": cb["unit"], "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "higher_is_better": True,
+            "scaling": "strong" if name in ENCODER_WORKLOADS else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "impl": "reference", "config": cfg, "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="default",
+                    help="default = mt5_c2 headline with the DeBERTa C1 attention and C3 encoder lines "
+                         "as sub-results; or one of the named workloads")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sub-results", action="store_true")
+    args = ap.parse_args()
+    warmup = max(args.warmup, 3)
+    headline = "mt5_c2" if args.workload == "default" else args.workload
+    subs = args.workload == "default" and not args.no_sub_results
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        line = reference_line(args, headline)
+        if subs:
+            line["sub_results"] = {"deberta_c1": reference_line(args, "deberta_c1_fused"),
+                                   "deberta_c3": reference_line(args, "deberta_c3")}
+        print(json.dumps(line))
+        return
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA GPU")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     if world > 1:
+        import datetime
+        # NCCL's initialisation log (communicator ranks) goes to stderr; rank 0's stdout
+        # carries only the JSON line.  A caller's own NCCL_DEBUG settings are kept.
+        if "NCCL_DEBUG" not in os.environ:
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    import vf_b200
+    vf_b200.load()
+    cpu_base = not args.no_cpu_baseline
+
+    if headline in ENCODER_WORKLOADS:
+        line = run_encoder(args, headline, args.steps, world, rank, dev, warmup, cpu_base)
+    elif headline == "mt5_ffn_act":
+        line = run_gated_act(args, world, rank, dev, warmup)
+    elif headline == "deberta_add_ln":
+        line = run_add_layer_norm(args, world, rank, dev, warmup)
+    else:
+        line = run_attention(args, headline, args.steps, world, rank, dev, warmup, cpu_base)
+    if subs:
+        # Same run, same ranks: the DeBERTa attention layer (weak-scaled like the headline)
+        # and the 24-layer DeBERTa encoder (strong-scaled by LPT over the ranks).
+        sub_steps = max(3, min(args.steps, 20))
+        d1 = run_attention(args, deberta_line_workload(), args.steps, world, rank, dev, warmup, cpu_base)
+        c3 = run_encoder(args, "deberta_c3", sub_steps, world, rank, dev, warmup, cpu_base)
+        if line is not None:
+            line["sub_results"] = {"deberta_c1": d1, "deberta_c3": c3}
+            line["gpu_launches"] += d1["gpu_launches"] + c3["gpu_launches"]
+    if line is not None:
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
 

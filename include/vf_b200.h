@@ -10,7 +10,7 @@
  * The reference (vllm-factory 0.2.2) has no native layer: its two hot-path operators
  * are Python launchers of Triton kernels.  Each entry point below names the Python
  * interface it replaces, and the ctypes binding in vllm-factory_b200/vf_b200/_lib.py is
- * the binding a maintainer of the reference would add (see INTEGRATION.md).
+ * the binding a maintainer of the reference would add.
  */
 #ifndef VF_B200_H_
 #define VF_B200_H_
@@ -19,6 +19,11 @@
 
 #ifdef __cplusplus
 extern "C" {
+#endif
+
+/* The library is built with hidden visibility; exactly the entry points below are exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
 #endif
 
 #define VF_ABI_VERSION 1
@@ -221,6 +226,10 @@ int vf_selftest_wait_timeout(int64_t limit_cycles, void* stream);
 
 /* VF_ABI_VERSION of the loaded library. */
 int vf_abi_version(void);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
 
 #ifdef __cplusplus
 }

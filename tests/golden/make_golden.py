@@ -50,9 +50,12 @@ def _bootstrap_vllm_cpu():
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("VF_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("VF_REFERENCE"),
+                    help="path of a vllm-factory checkout (default: $VF_REFERENCE)")
     ap.add_argument("--out", default=str(HERE / "golden.npz"))
     args = ap.parse_args()
+    if not args.reference:
+        raise SystemExit("make_golden.py needs a reference checkout: pass --reference or set VF_REFERENCE")
     sys.path.insert(0, args.reference)
     torch.set_num_threads(os.cpu_count() or 1)
     out = {}

@@ -42,3 +42,21 @@ def test_traffic_entries_for_captured_workloads():
     t = json.loads((ROOT / "profiles" / "traffic.json").read_text())
     for w in ("mt5_c2", "deberta_c1", "mt5_c2_varlen", "deberta_c1_varlen", "mt5_ffn_act", "deberta_add_ln"):
         assert isinstance(t.get(w), int) and t[w] > 0, w
+
+
+def test_reference_arm_default_has_same_configs_and_sub_results():
+    """The default run's reference line carries the headline and both sub-results, each with
+    the `config` object the GPU arm prints for the same workload."""
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "vllm-factory_b200"))
+    import bench
+    lines = _run(["--impl", "reference", "--steps", "3", "--warmup", "3"], timeout=400)
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["config"] == bench.attention_config("mt5_c2")
+    subs = d["sub_results"]
+    assert subs["deberta_c1"]["config"] == bench.attention_config("deberta_c1_fused")
+    assert subs["deberta_c3"]["config"] == bench.attention_config("deberta_c3")
+    assert subs["deberta_c3"]["unit"] == "tokens/s per layer" and subs["deberta_c3"]["scaling"] == "strong"
+    for s in subs.values():
+        assert s["impl"] == "reference" and s["value"] > 0

@@ -146,7 +146,7 @@ def test_deberta_c1_config_subset():
 
 
 def test_deberta_fp32_inputs_tf32_level():
-    """fp32 inputs (BASELINE C1's dtype): fp16 operands, fp32 softmax/accumulation, fp32 out."""
+    """fp32 inputs (the C1 workload's dtype: 8 x 512, U[64,512]): fp16 operands, fp32 softmax/accumulation, fp32 out."""
     q, k, v, pk, pq, sl = make(2, 2, 320, 320, 256, dtype=torch.float32, lens=[320, 200], seed=23)
     dev = torch.device("cuda")
     cu = lambda t: None if t is None else t.to(dev)

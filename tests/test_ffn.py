@@ -74,3 +74,14 @@ def test_oracle_without_up_is_the_activation(act):
     """up = None: the plain activation (the DeBERTa feed-forward uses the exact GELU)."""
     g = torch.randn(64, 96, generator=torch.Generator().manual_seed(act)) * 3
     torch.testing.assert_close(oracle.gated_act_ref(g, None, act), FALLBACK[act](g), rtol=2e-6, atol=1e-5)
+
+
+def test_gated_act_without_up_argument_rules():
+    """up = NULL (activation only): any up_row_stride is accepted (it is not read), an empty
+    call returns VF_OK, and a NULL gate or out is still refused before any launch."""
+    lib = _lib.load()
+    assert lib.vf_gated_act_fwd(ctypes.byref(_args(up=None, up_row_stride=0, rows=0)), None) == _lib.VF_OK
+    assert lib.vf_gated_act_fwd(ctypes.byref(_args(up=None, up_row_stride=-5, rows=0)), None) == _lib.VF_OK
+    assert lib.vf_gated_act_fwd(ctypes.byref(_args(gate=None, up=None)), None) == _lib.VF_EINVAL
+    assert "non-null" in lib.vf_last_error().decode()
+    assert lib.vf_gated_act_fwd(ctypes.byref(_args(out=None, up=None)), None) == _lib.VF_EINVAL

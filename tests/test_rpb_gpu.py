@@ -118,7 +118,7 @@ def test_rpb_golden_reference_case():
 
 
 def test_rpb_c2_config_subset():
-    # BASELINE config C2 shape (B=16, L=768, H=16, D=64, 32 buckets / 128) with ragged
+    # The C2 workload's shape (B=16, L=768, H=16, D=64, 32 buckets / 128) with ragged
     # lengths; the oracle checks two batch rows to bound CPU time.
     from vf_b200.workloads import mt5_attention_inputs
     w = mt5_attention_inputs(seed=0, device="cuda")

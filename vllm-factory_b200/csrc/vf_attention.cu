@@ -984,6 +984,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
         const float inv_l = use ? 1.f / l_run : 0.f;
         bulk_wait_read_all();                // this thread's previous row copy has read its row
         uint8_t* srow = smem + S::kOffOStage + g * kTileBytes + row * 128;
+        // The row's eight 16-byte chunks, packed.  Written in natural order, the 8 lanes of
+        // one store phase (rows r..r+7, 128 bytes apart) would all hit the same four banks;
+        // instead step s writes chunk s ^ (row & 7), so those lanes write 8 different
+        // chunks.  pk[s] is brought to hold chunk s ^ (row & 7) by three conditional swaps.
+        uint4 pk[kHeadDim / 8];
 #pragma unroll
         for (int ch = 0; ch < kHeadDim / 16; ++ch) {
           uint32_t o[16];
@@ -998,13 +1003,28 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             float f[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) f[j] = use ? __uint_as_float(o[8 * hf + j]) * inv_l : 0.f;
-            uint4 v;
+            uint4& v = pk[2 * ch + hf];
             v.x = pack2<T>(f[0], f[1]);
             v.y = pack2<T>(f[2], f[3]);
             v.z = pack2<T>(f[4], f[5]);
             v.w = pack2<T>(f[6], f[7]);
-            if (mine) *reinterpret_cast<uint4*>(srow + (2 * ch + hf) * 16) = v;
           }
+        }
+        const int rx = row & 7;
+#pragma unroll
+        for (int bit = 1; bit < 8; bit <<= 1) {
+          const bool sw = (rx & bit) != 0;
+#pragma unroll
+          for (int s = 0; s < 8; ++s) {
+            if ((s & bit) != 0) continue;
+            const uint4 a = pk[s], b = pk[s | bit];
+            pk[s] = sw ? b : a;
+            pk[s | bit] = sw ? a : b;
+          }
+        }
+        if (mine) {
+#pragma unroll
+          for (int s = 0; s < 8; ++s) *reinterpret_cast<uint4*>(srow + ((s ^ rx) * 16)) = pk[s];
         }
         if (mine) {
           fence_proxy_async_smem();
@@ -1425,13 +1445,8 @@ int vf_device_error(int32_t clear) {
   unsigned int word = 0;
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return fail(VF_ECUDA, std::string("cudaDeviceSynchronize: ") + cudaGetErrorString(e));
-  e = cudaMemcpyFromSymbol(&word, vf::g_vf_error, sizeof(word));
-  if (e != cudaSuccess) return fail(VF_ECUDA, std::string("cudaMemcpyFromSymbol: ") + cudaGetErrorString(e));
-  if (clear) {
-    const unsigned int zero = 0;
-    e = cudaMemcpyToSymbol(vf::g_vf_error, &zero, sizeof(zero));
-    if (e != cudaSuccess) return fail(VF_ECUDA, std::string("cudaMemcpyToSymbol: ") + cudaGetErrorString(e));
-  }
+  e = vf::take_error_word(clear != 0, &word);
+  if (e != cudaSuccess) return fail(VF_ECUDA, std::string("reading the device error word: ") + cudaGetErrorString(e));
   return static_cast<int>(word & 0x7fffffff);
 }
 

@@ -4,12 +4,21 @@
 #pragma once
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_runtime.h>
 
 namespace vf {
 
-// Device-wide error word.  Kernels OR error bits into it (a bounded wait that ran out,
-// an index that failed a check); the host reads it back with vf_device_error().
-__device__ unsigned int g_vf_error;
+// Device-wide error word of this translation unit.  Kernels OR error bits into it (a
+// bounded wait that ran out, an index that failed a check); the host takes it with
+// take_error_word() (vf_device_error() gathers the words of every kernel file).
+static __device__ unsigned int g_vf_error;
+static __device__ unsigned int g_vf_error_taken;
+
+// Reads the word and, with `clear`, zeroes it in the same atomic operation, so a bit that a
+// kernel on another stream sets meanwhile is either taken now or stays for the next call.
+static __global__ void take_error_word_kernel(int clear) {
+  g_vf_error_taken = clear ? atomicExch(&g_vf_error, 0u) : atomicOr(&g_vf_error, 0u);
+}
 
 enum : unsigned int {
   kErrWaitTimeout = 1u << 0,   // an mbarrier wait exceeded its cycle budget
@@ -374,6 +383,15 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
 // Arrives on a named barrier without waiting (the producer side of a hand-over).
 __device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.arrive %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+
+// Host side of take_error_word_kernel: one launch on the legacy default stream and a read
+// of the result.  Returns the cudaError_t of the first failing call.
+static inline cudaError_t take_error_word(bool clear, unsigned int* word) {
+  take_error_word_kernel<<<1, 1, 0, 0>>>(clear ? 1 : 0);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyFromSymbol(word, g_vf_error_taken, sizeof(unsigned int));
 }
 
 }  // namespace vf

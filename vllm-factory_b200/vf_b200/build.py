@@ -25,7 +25,7 @@ TORCH_DEPS = TORCH_SOURCES + [INCLUDE / "vf_b200.h"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-std=c++17", "-lineinfo",
-    "-Xcompiler", "-fPIC,-O2",
+    "-Xcompiler", "-fPIC,-O2,-fvisibility=hidden",
     "-shared",
 ]
 
@@ -60,7 +60,11 @@ def build_torch_ops(force: bool = False, verbose: bool = False) -> Path:
     incs = [f"-I{p}" for p in ce.include_paths(device_type="cuda")] + [f"-I{INCLUDE}"]
     libdirs = ce.library_paths(device_type="cuda")
     tmp = TORCH_LIB_PATH.with_suffix(".so.tmp")
-    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+    # The flags torch.utils.cpp_extension gives an extension (same compiler family as torch's
+    # own build: GCC 13), with hidden visibility so that no template instantiation of this
+    # library interposes on torch's.
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-DTORCH_API_INCLUDE_EXTENSION_H",
            *incs, *map(str, TORCH_SOURCES), "-o", str(tmp),
            *[f"-L{d}" for d in libdirs], "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda",
            f"-L{PKG_DIR}", "-lvf_b200", "-Wl,-rpath,$ORIGIN"]

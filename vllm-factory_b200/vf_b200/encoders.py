@@ -146,6 +146,10 @@ class DebertaV3Encoder:
         E, F_ = self.cfg.hidden, self.cfg.ffn
         return self.cfg.layers * 2.0 * (4 * E * E + 2 * E * F_)
 
+    def own_launches_per_layer(self) -> int:
+        """This package's kernel launches per layer: the attention and two add + LayerNorm."""
+        return 3
+
 
 class MT5Encoder:
     """mT5 encoder over a packed batch; attention = flash_attention_rpb_varlen and the
@@ -194,6 +198,10 @@ class MT5Encoder:
     def flops_per_token_gemm(self) -> float:
         E, F_ = self.cfg.hidden, self.cfg.ffn
         return self.cfg.layers * 2.0 * (4 * E * E + 3 * E * F_)
+
+    def own_launches_per_layer(self) -> int:
+        """This package's kernel launches per layer: the attention and the gated activation."""
+        return 2
 
 
 def packed_batch(n_seqs: int, lo: int, hi: int, vocab: int, seed: int = 0):

@@ -152,3 +152,17 @@ def deberta_varlen_inputs(seed: int = 0, device="cuda", B: int = 8, L: int = 512
     out.update(q=pack(w["q"]), k=pack(w["k"]), v=pack(w["v"]), pos_key=pack(w["pos_key"]),
                pos_query=pack(w["pos_query"]), cu_seqlens=cu.to(w["q"].device), max_seqlen=max(lens))
     return out
+
+
+def rank_lengths(kind: str, rank: int):
+    """Valid lengths of rank `rank`'s batch in a weak-scaled attention run: every rank gets
+    the lengths of rank 0's seeded batch (seed 1000 for C2, 2000 for C1), rotated by the
+    rank, so each rank does the same valid work on its own data.  None for rank 0, whose
+    batch draws them itself (the seeded single-GPU input)."""
+    if rank == 0:
+        return None
+    if kind == "mt5":
+        base = torch.randint(256, 768 + 1, (16,), generator=_gen(1000))
+    else:
+        base = torch.randint(64, 512 + 1, (8,), generator=_gen(2000))
+    return torch.roll(base, shifts=rank)
