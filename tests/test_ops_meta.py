@@ -44,3 +44,12 @@ def test_cpu_tensors_raise():
                  lambda: OPS.add_layer_norm(qp, qp, qp[0, 0], None, 1e-7)):
         with pytest.raises(RuntimeError, match="CUDA"):
             call()
+
+
+def test_op_layer_uses_the_shared_cxx_runtime():
+    """The torch op layer must not carry its own libstdc++: with a private copy (a toolchain
+    that links libstdc++.a), formatting a number into a TORCH_CHECK message crashed the
+    process on the duplicated locale facets instead of raising RuntimeError."""
+    from vf_b200 import build
+    assert build.embedded_cxx_runtime(build.TORCH_LIB_PATH) == []
+    assert build.embedded_cxx_runtime(build.LIB_PATH) == []

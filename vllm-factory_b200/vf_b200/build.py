@@ -48,6 +48,28 @@ def is_stale() -> bool:
     return _stale(LIB_PATH, DEPS) or _stale(TORCH_LIB_PATH, TORCH_DEPS + [LIB_PATH])
 
 
+def system_cxx() -> str:
+    """The C++ compiler for the torch op layer: VF_CXX if set, else the system g++ (the GCC
+    13 that torch itself was built with, linking the shared libstdc++.so.6).  $CXX is not
+    used: a toolchain that links libstdc++ statically into the library gives the process a
+    second copy of the C++ runtime, and then formatting a number into an exception message
+    (any TORCH_CHECK with a value in its text) crashes on the duplicated locale facets."""
+    cand = os.environ.get("VF_CXX") or shutil.which("g++", path="/usr/bin:/bin") or shutil.which("g++")
+    if not cand:
+        raise RuntimeError("no C++ compiler found for the torch op layer (set VF_CXX)")
+    return cand
+
+
+def embedded_cxx_runtime(lib: Path) -> list[str]:
+    """libstdc++ internals that `lib` defines itself (empty for a library that uses the
+    process's shared libstdc++.so.6)."""
+    res = subprocess.run(["nm", "-D", "-C", "--defined-only", str(lib)], capture_output=True, text=True)
+    if res.returncode != 0:
+        return []
+    bad = ("std::locale::id::_M_id", "std::locale::facet::_M_cow_shim", "std::ios_base::Init::Init")
+    return [l for l in res.stdout.splitlines() if any(b in l for b in bad)]
+
+
 def build_torch_ops(force: bool = False, verbose: bool = False) -> Path:
     """Compiles the torch op layer (csrc/vf_torch_ops.cpp) against torch's headers and the
     C ABI library; the result is loaded with torch.ops.load_library."""
@@ -55,7 +77,7 @@ def build_torch_ops(force: bool = False, verbose: bool = False) -> Path:
         return TORCH_LIB_PATH
     import torch
     from torch.utils import cpp_extension as ce
-    cxx = os.environ.get("CXX", shutil.which("g++") or "c++")
+    cxx = system_cxx()
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     incs = [f"-I{p}" for p in ce.include_paths(device_type="cuda")] + [f"-I{INCLUDE}"]
     libdirs = ce.library_paths(device_type="cuda")
@@ -73,6 +95,11 @@ def build_torch_ops(force: bool = False, verbose: bool = False) -> Path:
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"torch op layer build failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    embedded = embedded_cxx_runtime(tmp)
+    if embedded:
+        tmp.unlink()
+        raise RuntimeError(f"{cxx} linked its own copy of libstdc++ into the torch op layer "
+                           f"(e.g. {embedded[0].strip()}); build with the system g++ (VF_CXX)")
     os.replace(tmp, TORCH_LIB_PATH)
     return TORCH_LIB_PATH
 
