@@ -143,6 +143,56 @@ int vf_deberta_attention_varlen_fwd(const vf_deberta_attention_args_t* args, con
                                     int32_t num_seqs, int32_t max_seqlen, void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * DeBERTa disentangled attention with the position contractions inside the kernel (the
+ * "fused" mode).  Same operator as vf_deberta_attention_fwd, but the caller passes the
+ * projected position tables instead of their products with q and k:
+ *   rel_key   = key_proj(rel_embeddings)   as (1, H, 2S, 64)   (Kr)
+ *   rel_query = query_proj(rel_embeddings) as (1, H, 2S, 64)   (Qr)
+ * and the kernel forms pos_key[m, idx] = q[m]·Kr[idx] and pos_query[n, idx] = k[n]·Qr[idx]
+ * on the tensor cores, tile by tile, so the two (B, H, L, 2S) tensors of
+ * models/deberta_v2/deberta_v2_encoder.py:275-286 are never built.  Replaces that caller's
+ * two torch.matmul products together with kernels/flash_deberta_attention.py:455; the
+ * reference has no fused entry point.
+ *
+ * q, k, v, out, seq_lengths, causal, sm_scale, position_buckets, max_relative_distance,
+ * use_log_bucket: as vf_deberta_attention_args_t.  rel_key / rel_query: 16-bit views of the
+ * dtype of q, size (1, H, >= 2S, 64), unit innermost stride, 16-byte aligned rows; data NULL
+ * = that term absent.  Sequences of at most 65536 positions.
+ * workspace: device scratch of at least vf_deberta_fused_workspace_bytes() bytes, 256-byte
+ * aligned, owned by the caller, only used by the call's own kernels (a call on another
+ * stream needs its own).  It holds the position tables expanded to one row per relative
+ * position (2 x H x (ceil128(M) + ceil128(N)) x 64 elements) and the unit order.
+ * ------------------------------------------------------------------------------------ */
+typedef struct {
+  vf_dtype_t dtype;
+  vf_tensor4d_t q, k, v;
+  vf_tensor4d_t out;
+  const int32_t* seq_lengths;
+  vf_tensor4d_t rel_key, rel_query;
+  int32_t causal;
+  int32_t has_sm_scale;
+  float sm_scale;
+  int32_t position_buckets;
+  int32_t max_relative_distance;
+  int32_t use_log_bucket;
+} vf_deberta_fused_args_t;
+
+/* Workspace bytes of the fused entry points: batch rows (or packed sequences), heads and the
+ * query / key lengths (max_seqlen for the packed form).  Negative VF_E* code on bad sizes. */
+int64_t vf_deberta_fused_workspace_bytes(int64_t batch_or_seqs, int64_t heads, int64_t M, int64_t N);
+
+int vf_deberta_attention_fused_fwd(const vf_deberta_fused_args_t* args, void* workspace, int64_t workspace_bytes,
+                                   void* stream);
+
+/* Packed variable-length batch of the fused operator: q, k, v, out are (1, H, total, 64)
+ * views, sequence s is rows [cu_seqlens[s], cu_seqlens[s+1]) and attends within itself;
+ * seq_lengths must be NULL; cu_seqlens / num_seqs / max_seqlen as for
+ * vf_deberta_attention_varlen_fwd.  Rows of out outside every sequence are not written. */
+int vf_deberta_attention_fused_varlen_fwd(const vf_deberta_fused_args_t* args, const int32_t* cu_seqlens,
+                                          int32_t num_seqs, int32_t max_seqlen, void* workspace,
+                                          int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Gated activation of the mT5 feed-forward: out = act(gate) * up, in fp32, rounded to the
  * dtype.  Replaces kernels/ff_fused.py:86 `fused_gelu_mul_dropout(gate, up, act_fn,
  * dropout_p, training)` and its kernel (:23-74) on the inference path (no dropout).

@@ -17,6 +17,7 @@ It restates, in plain PyTorch on the CPU, the reference's own algorithms for the
                       :295-299, :334); the packed form applies it to each cu_seqlens
                       sequence alone
   * DeBERTa layer:    models/deberta_v2/deberta_v2_encoder.py:332-487 (_pytorch_forward)
+  * DeBERTa fused:    the caller's products q @ Kr^T, k @ Qr^T (:275-286) + the op above
   * mT5 FFN act:      kernels/ff_fused.py:23-74 (fused_gelu_mul_dropout's kernel, no dropout)
 
 Parity pinning: tests/golden/make_golden.py runs the reference's own functions (imported
@@ -24,6 +25,8 @@ from the read-only reference checkout in the build container) and commits their 
 under tests/golden/; tests/test_oracle_golden.py checks this oracle against them.
 """
 from .rpb import (  # noqa: F401
+    deberta_attention_fused_ref,
+    deberta_attention_fused_varlen_ref,
     deberta_attention_ref,
     deberta_attention_varlen_ref,
     deberta_layer_ref,

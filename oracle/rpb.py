@@ -175,6 +175,49 @@ def deberta_attention_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return out
 
 
+def deberta_attention_fused_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                                seq_lengths: Optional[torch.Tensor] = None,
+                                rel_key: Optional[torch.Tensor] = None,
+                                rel_query: Optional[torch.Tensor] = None,
+                                causal: bool = False, sm_scale: Optional[float] = None,
+                                position_buckets: int = 0, max_relative_distance: int = 0,
+                                use_log_bucket: bool = False, dtype=torch.float64) -> torch.Tensor:
+    """The fused position mode: the caller's products of
+    models/deberta_v2/deberta_v2_encoder.py:279 / :284-286, pos_key = q @ Kr^T and
+    pos_query = k @ Qr^T, formed here in `dtype` (not rounded to the input dtype as the
+    reference's torch.matmul does), then deberta_attention_ref.  rel_key / rel_query:
+    (1, H, 2S, D) or (H, 2S, D)."""
+    def prod(x, r):
+        if r is None:
+            return None
+        r = r if r.dim() == 4 else r.unsqueeze(0)
+        return torch.matmul(x.to(dtype), r.to(dtype).transpose(-1, -2))
+    return deberta_attention_ref(q, k, v, seq_lengths, prod(q, rel_key), prod(k, rel_query), causal, sm_scale,
+                                 position_buckets, max_relative_distance, use_log_bucket, dtype=dtype)
+
+
+def deberta_attention_fused_varlen_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens,
+                                       rel_key: Optional[torch.Tensor] = None,
+                                       rel_query: Optional[torch.Tensor] = None,
+                                       causal: bool = False, sm_scale: Optional[float] = None,
+                                       position_buckets: int = 0, max_relative_distance: int = 0,
+                                       use_log_bucket: bool = False, dtype=torch.float64,
+                                       fill: float = float("nan")) -> torch.Tensor:
+    """Packed form of deberta_attention_fused_ref: q, k, v [total, H, D]; each cu_seqlens
+    sequence alone; rows outside every sequence are `fill`."""
+    cu = [int(x) for x in torch.as_tensor(cu_seqlens).tolist()]
+    out = torch.full(q.shape, fill, dtype=dtype)
+    for s in range(len(cu) - 1):
+        a, b = cu[s], cu[s + 1]
+        if b <= a:
+            continue
+        seq = lambda t: t[a:b].permute(1, 0, 2).unsqueeze(0)
+        o = deberta_attention_fused_ref(seq(q), seq(k), seq(v), None, rel_key, rel_query, causal, sm_scale,
+                                        position_buckets, max_relative_distance, use_log_bucket, dtype=dtype)
+        out[a:b] = o[0].permute(1, 0, 2)
+    return out
+
+
 def deberta_attention_varlen_ref(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens,
                                  pos_key: Optional[torch.Tensor] = None,
                                  pos_query: Optional[torch.Tensor] = None,

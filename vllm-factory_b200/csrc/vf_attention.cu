@@ -44,6 +44,7 @@
 #include <vector>
 
 #include "vf_ptx.cuh"
+#include "vf_internal.h"
 #include "../../include/vf_b200.h"
 
 namespace vf {
@@ -1431,8 +1432,26 @@ int finish_deberta_table(const vf_deberta_attention_args_t* a, int span_rows, vf
 }  // namespace
 
 namespace vf {
-// The thread's last error message, for the other translation units of the library.
-__attribute__((visibility("hidden"))) int set_last_error(int code, const std::string& msg) { return fail(code, msg); }
+// Host helpers for the other kernel files of the library (vf_internal.h).
+int set_last_error(int code, const std::string& msg) { return fail(code, msg); }
+int host_make_tile_map(CUtensorMap* map, const vf_tensor4d_t& t, vf_dtype_t dt, const char* name) {
+  return make_tile_map(map, t, dt, name);
+}
+int host_check_qkv(const vf_tensor4d_t& q, const vf_tensor4d_t& k, const vf_tensor4d_t& v, const vf_tensor4d_t& o) {
+  return check_qkv(q, k, v, o);
+}
+int host_check_packed(const vf_tensor4d_t& q, const vf_tensor4d_t& k, const int32_t* cu_seqlens, int32_t num_seqs,
+                      int32_t max_seqlen, const char* what) {
+  return check_packed(q, k, cu_seqlens, num_seqs, max_seqlen, what);
+}
+int host_deberta_index_table(int span, int position_buckets, int max_relative_distance, bool log_bucket, int L,
+                             int max_radius, short* lut_out) {
+  const RelTable& tab = deberta_table(span, position_buckets, max_relative_distance, log_bucket, L);
+  if (tab.R > max_radius) return -1;
+  std::memcpy(lut_out, tab.lut.data(), tab.lut.size() * sizeof(short));
+  return tab.R;
+}
+PFN_cuTensorMapEncodeTiled_v12000 host_encode_fn() { return get_encode_fn(); }
 }  // namespace vf
 
 extern "C" {
@@ -1447,7 +1466,10 @@ int vf_device_error(int32_t clear) {
   if (e != cudaSuccess) return fail(VF_ECUDA, std::string("cudaDeviceSynchronize: ") + cudaGetErrorString(e));
   e = vf::take_error_word(clear != 0, &word);
   if (e != cudaSuccess) return fail(VF_ECUDA, std::string("reading the device error word: ") + cudaGetErrorString(e));
-  return static_cast<int>(word & 0x7fffffff);
+  unsigned int fused_word = 0;
+  e = vf::fused_take_error_word(clear != 0, &fused_word);
+  if (e != cudaSuccess) return fail(VF_ECUDA, std::string("reading the device error word: ") + cudaGetErrorString(e));
+  return static_cast<int>((word | fused_word) & 0x7fffffff);
 }
 
 int vf_selftest_wait_timeout(int64_t limit_cycles, void* stream) {

@@ -307,6 +307,131 @@ at::Tensor deberta_attention_varlen(const at::Tensor& q_in, const at::Tensor& k_
   return f32 ? out.to(at::kFloat) : out;
 }
 
+// Fused DeBERTa mode: rel_key / rel_query (1, H, 2S, 64) in place of pos_key / pos_query; the
+// position products run inside the kernel.  The workspace (expanded position tables and
+// the unit order) comes from the caching allocator on the call's stream.
+at::Tensor rel_ready(const std::optional<at::Tensor>& t, const at::Tensor& q_in, const char* name) {
+  if (!t.has_value() || !t->defined()) return at::Tensor();
+  require_cuda(*t, name);
+  TORCH_CHECK(t->scalar_type() == q_in.scalar_type(), "vf_b200: ", name, " must have the dtype of q");
+  at::Tensor x = *t;
+  if (x.dim() == 3) x = x.unsqueeze(0);
+  TORCH_CHECK(x.dim() == 4, "vf_b200: ", name, " must be (1, H, 2*span, 64) or (H, 2*span, 64)");
+  x = to_kernel_dtype(x);
+  const int64_t es = x.element_size();
+  if (x.stride(3) != 1 || (x.stride(2) * es) % 16 != 0 || (x.stride(1) * es) % 16 != 0 ||
+      (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) != 0)
+    x = x.contiguous();
+  return x;
+}
+
+vf_tensor4d_t view4_or_absent(const at::Tensor& t) { return t.defined() ? view4(t) : vf_tensor4d_t{}; }
+
+at::Tensor deberta_attention_fused(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
+                                   const std::optional<at::Tensor>& seq_lengths,
+                                   const std::optional<at::Tensor>& rel_key,
+                                   const std::optional<at::Tensor>& rel_query, bool causal,
+                                   std::optional<double> sm_scale, int64_t position_buckets,
+                                   int64_t max_relative_distance, bool use_log_bucket) {
+  require_cuda(q_in, "q");
+  require_cuda(k_in, "k");
+  require_cuda(v_in, "v");
+  TORCH_CHECK(q_in.scalar_type() == k_in.scalar_type() && q_in.scalar_type() == v_in.scalar_type(),
+              "vf_b200: q, k, v must share a dtype");
+  c10::cuda::CUDAGuard guard(q_in.device());
+  const bool f32 = q_in.scalar_type() == at::kFloat;
+  const at::Tensor q = tma_ready(to_kernel_dtype(q_in)), k = tma_ready(to_kernel_dtype(k_in)),
+                   v = tma_ready(to_kernel_dtype(v_in));
+  at::Tensor out = make_out(q);
+  const at::Tensor rk = rel_ready(rel_key, q_in, "rel_key"), rq = rel_ready(rel_query, q_in, "rel_query");
+  vf_deberta_fused_args_t a{};
+  a.dtype = dtype_code(q);
+  a.q = view4(q);
+  a.k = view4(k);
+  a.v = view4(v);
+  a.out = view4(out);
+  at::Tensor lens;
+  if (seq_lengths.has_value()) {
+    require_cuda(*seq_lengths, "seq_lengths");
+    lens = *seq_lengths;
+    if (lens.scalar_type() != at::kInt || !lens.is_contiguous()) lens = lens.to(at::kInt).contiguous();
+    TORCH_CHECK(lens.numel() == q.size(0), "vf_b200: seq_lengths must have one entry per batch row");
+    a.seq_lengths = lens.data_ptr<int32_t>();
+  }
+  a.rel_key = view4_or_absent(rk);
+  a.rel_query = view4_or_absent(rq);
+  a.causal = causal ? 1 : 0;
+  a.has_sm_scale = sm_scale.has_value() ? 1 : 0;
+  a.sm_scale = sm_scale.has_value() ? static_cast<float>(*sm_scale) : 0.f;
+  a.position_buckets = static_cast<int32_t>(position_buckets);
+  a.max_relative_distance = static_cast<int32_t>(max_relative_distance);
+  a.use_log_bucket = use_log_bucket ? 1 : 0;
+  const int64_t ws_bytes = vf_deberta_fused_workspace_bytes(q.size(0), q.size(1), q.size(2), k.size(2));
+  check_rc(ws_bytes < 0 ? static_cast<int>(ws_bytes) : VF_OK);
+  at::Tensor ws = at::empty({ws_bytes + 256}, q.options().dtype(at::kByte));
+  void* ws_ptr = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ws.data_ptr()) + 255) & ~uintptr_t(255));
+  check_rc(vf_deberta_attention_fused_fwd(&a, ws_ptr, ws_bytes, at::cuda::getCurrentCUDAStream().stream()));
+  return f32 ? out.to(at::kFloat) : out;
+}
+
+// Packed fused DeBERTa batch: q, k, v [total, H, 64]; rel_key / rel_query (1, H, 2S, 64).
+at::Tensor deberta_attention_fused_varlen(const at::Tensor& q_in, const at::Tensor& k_in, const at::Tensor& v_in,
+                                          const at::Tensor& cu_seqlens, int64_t max_seqlen,
+                                          const std::optional<at::Tensor>& rel_key,
+                                          const std::optional<at::Tensor>& rel_query, bool causal,
+                                          std::optional<double> sm_scale, int64_t position_buckets,
+                                          int64_t max_relative_distance, bool use_log_bucket) {
+  require_cuda(q_in, "q");
+  require_cuda(k_in, "k");
+  require_cuda(v_in, "v");
+  TORCH_CHECK(q_in.dim() == 3 && k_in.dim() == 3 && v_in.dim() == 3, "vf_b200: packed q, k, v must be [total, heads, 64]");
+  TORCH_CHECK(q_in.scalar_type() == k_in.scalar_type() && q_in.scalar_type() == v_in.scalar_type(),
+              "vf_b200: q, k, v must share a dtype");
+  c10::cuda::CUDAGuard guard(q_in.device());
+  const bool f32 = q_in.scalar_type() == at::kFloat;
+  const at::Tensor q = packed_tma_ready(q_in), k = packed_tma_ready(k_in), v = packed_tma_ready(v_in);
+  at::Tensor out = at::empty(q.sizes(), q.options());
+  const at::Tensor cu = cu_int32(cu_seqlens);
+  const at::Tensor rk = rel_ready(rel_key, q_in, "rel_key"), rq = rel_ready(rel_query, q_in, "rel_query");
+  vf_deberta_fused_args_t a{};
+  a.dtype = dtype_code(q);
+  a.q = packed_view(q);
+  a.k = packed_view(k);
+  a.v = packed_view(v);
+  a.out = packed_view(out);
+  a.rel_key = view4_or_absent(rk);
+  a.rel_query = view4_or_absent(rq);
+  a.causal = causal ? 1 : 0;
+  a.has_sm_scale = sm_scale.has_value() ? 1 : 0;
+  a.sm_scale = sm_scale.has_value() ? static_cast<float>(*sm_scale) : 0.f;
+  a.position_buckets = static_cast<int32_t>(position_buckets);
+  a.max_relative_distance = static_cast<int32_t>(max_relative_distance);
+  a.use_log_bucket = use_log_bucket ? 1 : 0;
+  TORCH_CHECK(max_seqlen > 0 && max_seqlen <= INT32_MAX, "vf_b200: max_seqlen out of range");
+  const int64_t nseq = cu.numel() - 1;
+  const int64_t ws_bytes = vf_deberta_fused_workspace_bytes(nseq, q.size(1), max_seqlen, max_seqlen);
+  check_rc(ws_bytes < 0 ? static_cast<int>(ws_bytes) : VF_OK);
+  at::Tensor ws = at::empty({ws_bytes + 256}, q.options().dtype(at::kByte));
+  void* ws_ptr = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ws.data_ptr()) + 255) & ~uintptr_t(255));
+  check_rc(vf_deberta_attention_fused_varlen_fwd(&a, cu.data_ptr<int32_t>(), static_cast<int32_t>(nseq),
+                                                 static_cast<int32_t>(max_seqlen), ws_ptr, ws_bytes,
+                                                 at::cuda::getCurrentCUDAStream().stream()));
+  return f32 ? out.to(at::kFloat) : out;
+}
+
+at::Tensor deberta_attention_fused_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                       const std::optional<at::Tensor>&, const std::optional<at::Tensor>&,
+                                       const std::optional<at::Tensor>&, bool, std::optional<double>, int64_t,
+                                       int64_t, bool) {
+  TORCH_CHECK(false, "vf_b200: q, k, v must be CUDA tensors (no CPU implementation)");
+}
+at::Tensor deberta_attention_fused_varlen_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                              const at::Tensor&, int64_t, const std::optional<at::Tensor>&,
+                                              const std::optional<at::Tensor>&, bool, std::optional<double>,
+                                              int64_t, int64_t, bool) {
+  TORCH_CHECK(false, "vf_b200: q, k, v must be CUDA tensors (no CPU implementation)");
+}
+
 // Gated activation: out = act(gate) * up over the last dimension; leading dimensions are
 // rows.  Each operand only needs a unit stride on the last dimension and leading
 // dimensions that collapse to one row stride (as the two column halves of a 2-D [T, 2F]
@@ -475,6 +600,12 @@ TORCH_LIBRARY(vf_b200, m) {
   m.def("deberta_attention_varlen(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, int max_seqlen, Tensor? pos_key, "
         "Tensor? pos_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "
         "bool use_log_bucket) -> Tensor");
+  m.def("deberta_attention_fused(Tensor q, Tensor k, Tensor v, Tensor? seq_lengths, Tensor? rel_key, "
+        "Tensor? rel_query, bool causal, float? sm_scale, int position_buckets, int max_relative_distance, "
+        "bool use_log_bucket) -> Tensor");
+  m.def("deberta_attention_fused_varlen(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, int max_seqlen, "
+        "Tensor? rel_key, Tensor? rel_query, bool causal, float? sm_scale, int position_buckets, "
+        "int max_relative_distance, bool use_log_bucket) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, CUDA, m) {
@@ -482,6 +613,8 @@ TORCH_LIBRARY_IMPL(vf_b200, CUDA, m) {
   m.impl("rpb_attention_varlen", &rpb_attention_varlen);
   m.impl("deberta_attention", &deberta_attention);
   m.impl("deberta_attention_varlen", &deberta_attention_varlen);
+  m.impl("deberta_attention_fused", &deberta_attention_fused);
+  m.impl("deberta_attention_fused_varlen", &deberta_attention_fused_varlen);
   m.impl("gated_act", &gated_act);
   m.impl("add_layer_norm", &add_layer_norm);
 }
@@ -491,6 +624,8 @@ TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
   m.impl("rpb_attention_varlen", &rpb_attention_varlen_cpu);
   m.impl("deberta_attention", &deberta_attention_cpu);
   m.impl("deberta_attention_varlen", &deberta_attention_varlen_cpu);
+  m.impl("deberta_attention_fused", &deberta_attention_fused_cpu);
+  m.impl("deberta_attention_fused_varlen", &deberta_attention_fused_varlen_cpu);
   m.impl("gated_act", &gated_act_cpu);
   m.impl("add_layer_norm", &add_layer_norm_cpu);
 }
@@ -500,6 +635,8 @@ TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
   m.impl("rpb_attention_varlen", &rpb_attention_varlen_meta);
   m.impl("deberta_attention", &deberta_attention_meta);
   m.impl("deberta_attention_varlen", &deberta_attention_varlen_meta);
+  m.impl("deberta_attention_fused", &deberta_attention_meta);
+  m.impl("deberta_attention_fused_varlen", &deberta_attention_varlen_meta);
   m.impl("gated_act", &gated_act_meta);
   m.impl("add_layer_norm", &add_layer_norm_meta);
 }

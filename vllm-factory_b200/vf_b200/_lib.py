@@ -31,6 +31,9 @@ EXPORTED_SYMBOLS = (
     "vf_rpb_attention_varlen_fwd",
     "vf_deberta_attention_fwd",
     "vf_deberta_attention_varlen_fwd",
+    "vf_deberta_attention_fused_fwd",
+    "vf_deberta_attention_fused_varlen_fwd",
+    "vf_deberta_fused_workspace_bytes",
     "vf_gated_act_fwd",
     "vf_add_layer_norm_fwd",
     "vf_t5_relative_bucket",
@@ -127,6 +130,25 @@ class DebertaArgs(ctypes.Structure):
     ]
 
 
+class DebertaFusedArgs(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_int),
+        ("q", Tensor4d),
+        ("k", Tensor4d),
+        ("v", Tensor4d),
+        ("out", Tensor4d),
+        ("seq_lengths", ctypes.c_void_p),
+        ("rel_key", Tensor4d),
+        ("rel_query", Tensor4d),
+        ("causal", ctypes.c_int32),
+        ("has_sm_scale", ctypes.c_int32),
+        ("sm_scale", ctypes.c_float),
+        ("position_buckets", ctypes.c_int32),
+        ("max_relative_distance", ctypes.c_int32),
+        ("use_log_bucket", ctypes.c_int32),
+    ]
+
+
 class VfError(RuntimeError):
     """A libvf_b200 entry point returned an error code."""
 
@@ -162,6 +184,15 @@ def load() -> ctypes.CDLL:
         lib.vf_deberta_attention_varlen_fwd.argtypes = [ctypes.POINTER(DebertaArgs), ctypes.c_void_p,
                                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
         lib.vf_deberta_attention_varlen_fwd.restype = ctypes.c_int
+        lib.vf_deberta_fused_workspace_bytes.argtypes = [ctypes.c_int64] * 4
+        lib.vf_deberta_fused_workspace_bytes.restype = ctypes.c_int64
+        lib.vf_deberta_attention_fused_fwd.argtypes = [ctypes.POINTER(DebertaFusedArgs), ctypes.c_void_p,
+                                                       ctypes.c_int64, ctypes.c_void_p]
+        lib.vf_deberta_attention_fused_fwd.restype = ctypes.c_int
+        lib.vf_deberta_attention_fused_varlen_fwd.argtypes = [ctypes.POINTER(DebertaFusedArgs), ctypes.c_void_p,
+                                                              ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
+                                                              ctypes.c_int64, ctypes.c_void_p]
+        lib.vf_deberta_attention_fused_varlen_fwd.restype = ctypes.c_int
         lib.vf_gated_act_fwd.argtypes = [ctypes.POINTER(GatedActArgs), ctypes.c_void_p]
         lib.vf_gated_act_fwd.restype = ctypes.c_int
         lib.vf_add_layer_norm_fwd.argtypes = [ctypes.POINTER(AddLayerNormArgs), ctypes.c_void_p]

@@ -15,6 +15,11 @@ strides and the current CUDA stream and calls the C ABI of libvf_b200.so:
                                              pos_query?, causal, sm_scale?, position_buckets,
                                              max_relative_distance, use_log_bucket)   # packed
 
+  torch.ops.vf_b200.deberta_attention_fused(q, k, v, seq_lengths?, rel_key?, rel_query?, causal,
+                                            sm_scale?, position_buckets, max_relative_distance,
+                                            use_log_bucket)   # position products in the kernel
+  torch.ops.vf_b200.deberta_attention_fused_varlen(q, k, v, cu_seqlens, max_seqlen, rel_key?,
+                                                   rel_query?, ...)                    # packed
   torch.ops.vf_b200.gated_act(gate, up, act)                  # mT5 FFN: act(gate) * up (up=None: act(gate))
   torch.ops.vf_b200.add_layer_norm(x, residual, w, b, eps)   # DeBERTa: LayerNorm(x + residual)
 
@@ -42,5 +47,7 @@ rpb_attention = torch.ops.vf_b200.rpb_attention
 rpb_attention_varlen = torch.ops.vf_b200.rpb_attention_varlen
 deberta_attention = torch.ops.vf_b200.deberta_attention
 deberta_attention_varlen = torch.ops.vf_b200.deberta_attention_varlen
+deberta_attention_fused = torch.ops.vf_b200.deberta_attention_fused
+deberta_attention_fused_varlen = torch.ops.vf_b200.deberta_attention_fused_varlen
 gated_act = torch.ops.vf_b200.gated_act
 add_layer_norm = torch.ops.vf_b200.add_layer_norm
