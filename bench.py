@@ -415,6 +415,8 @@ def encoder_cpu_baseline(name: str, budget_s: float = 15.0):
     extra = ({"add_norm": lambda x, r, w, b, eps: oracle.add_layer_norm_ref(x, r, w, b, eps),
               "act_fn": lambda x: oracle.gated_act_ref(x, None, 1)} if name == "deberta_c3"
              else {"gated_act": lambda g, u, a: oracle.gated_act_ref(g, u, 0)})
+    if name == "deberta_c3":
+        extra["fused_positions"] = False   # the reference's caller forms q . Kr and k . Qr itself
     model = cls(small, device="cpu", dtype=torch.float32, seed=0, attention_fn=fn, **extra)
     done, n, t0 = 0, 0, time.perf_counter()
     while time.perf_counter() - t0 < budget_s and n < len(lengths):

@@ -15,6 +15,12 @@ def _deb_attn(q, k, v, cu, ms, pk, pq, c, sm, pb, mr, lg):
     return oracle.deberta_attention_varlen_ref(q, k, v, cu, pk, pq, c, sm, pb, mr, lg, dtype=torch.float32)
 
 
+def _deb_fused_attn(q, k, v, cu, ms, pk, pq, c, sm, pb, mr, lg, rel_key=None, rel_query=None):
+    assert pk is None and pq is None
+    return oracle.deberta_attention_fused_varlen_ref(q, k, v, cu, rel_key, rel_query, c, sm, pb, mr, lg,
+                                                     dtype=torch.float32)
+
+
 def _t5_attn(q, k, v, cu, ms, t, nb, md, dec, sc):
     return oracle.rpb_attention_varlen_ref(q, k, v, cu, t, nb, md, dec, sc, dtype=torch.float32)
 
@@ -39,7 +45,23 @@ def test_deberta_encoder_packing_invariance():
     cfg = dataclasses.replace(EN.DebertaConfig(), layers=2, hidden=128, heads=2, ffn=256, vocab=500,
                               position_buckets=16, max_relative_positions=64)
     _packing_invariance(EN.DebertaV3Encoder(cfg, device="cpu", dtype=torch.float32, attention_fn=_deb_attn,
-                                            add_norm=EN.add_layer_norm_torch, act_fn=F.gelu), 500)
+                                            add_norm=EN.add_layer_norm_torch, act_fn=F.gelu,
+                                            fused_positions=False), 500)
+
+
+def test_deberta_encoder_fused_positions_match_products():
+    """The fused mode's arguments (Kr, Qr as (H, 2S, D) views) give the same stack output as
+    the caller-side products (the reference's way) through the oracle."""
+    cfg = dataclasses.replace(EN.DebertaConfig(), layers=2, hidden=128, heads=2, ffn=256, vocab=500,
+                              position_buckets=16, max_relative_positions=64)
+    kw = dict(device="cpu", dtype=torch.float32, add_norm=EN.add_layer_norm_torch, act_fn=F.gelu)
+    fused = EN.DebertaV3Encoder(cfg, attention_fn=_deb_fused_attn, **kw)
+    compat = EN.DebertaV3Encoder(cfg, attention_fn=_deb_attn, fused_positions=False, **kw)
+    lengths, ids = EN.packed_batch(4, 3, 40, 500, seed=1)
+    x, cu, lens = EN.select_sequences(lengths, ids, range(4))
+    torch.testing.assert_close(fused.forward(x, cu, max(lens)), compat.forward(x, cu, max(lens)), atol=2e-5,
+                               rtol=2e-5)
+    _packing_invariance(fused, 500)
 
 
 def test_mt5_encoder_packing_invariance():
@@ -59,7 +81,7 @@ def test_deberta_position_scores_are_q_dot_kr():
         return _deb_attn(q, k, v, cu, ms, pk, pq, *rest)
 
     m = EN.DebertaV3Encoder(cfg, device="cpu", dtype=torch.float32, attention_fn=spy,
-                            add_norm=EN.add_layer_norm_torch, act_fn=F.gelu)
+                            add_norm=EN.add_layer_norm_torch, act_fn=F.gelu, fused_positions=False)
     lengths, ids = EN.packed_batch(2, 5, 9, 100, seed=2)
     x, cu, lens = EN.select_sequences(lengths, ids, range(2))
     m.forward(x, cu, max(lens))

@@ -25,12 +25,12 @@ def _t5_ref(q, k, v, cu, ms, t, nb, md, dec, sc):
     return o.to(q.dtype).to(q.device)
 
 
-def _compare(cls, cfg, ref_fn, lo, hi, what):
+def _compare(cls, cfg, ref_fn, lo, hi, what, **ref_kw):
     lengths, ids = EN.packed_batch(5, lo, hi, cfg.vocab, seed=3)
     x, cu, lens = EN.select_sequences(lengths, ids, range(5))
     x, cu = x.cuda(), cu.cuda()
     ours = cls(cfg, device="cuda", seed=0).forward(x, cu, max(lens))
-    ref = cls(cfg, device="cuda", seed=0, attention_fn=ref_fn).forward(x, cu, max(lens))
+    ref = cls(cfg, device="cuda", seed=0, attention_fn=ref_fn, **ref_kw).forward(x, cu, max(lens))
     torch.cuda.synchronize()
     assert torch.isfinite(ours.float()).all()
     # Only the attention differs; its bf16 rounding, carried through the residual stream,
@@ -42,7 +42,8 @@ def _compare(cls, cfg, ref_fn, lo, hi, what):
 
 def test_deberta_c3_stack_two_layers():
     cfg = dataclasses.replace(EN.DebertaConfig(), layers=2, vocab=4000)
-    _compare(EN.DebertaV3Encoder, cfg, _deb_ref, 100, 700, "C3 2 layers")
+    # ours: the fused position mode; reference: the caller-side products and the oracle
+    _compare(EN.DebertaV3Encoder, cfg, _deb_ref, 100, 700, "C3 2 layers", fused_positions=False)
 
 
 def test_mt5_c4_stack_two_layers():

@@ -18,13 +18,14 @@
 // add both tiles to S = Q K^T in TMEM.  The softmax warps see the finished score sum and
 // run a plain online softmax.  No (B, H, L, 2S) tensor exists anywhere.
 //
-// Warps (384 threads, 3 warpgroups):
+// Warps (512 threads, 4 warpgroups):
 //   0-3   softmax, one thread per query row (TMEM lane)
-//   4-7   position warps (warp 4 + s reads TMEM lanes 32 s .. 32 s + 31)
-//   8     TMA producer: Q per unit; K / V (2-stage rings), KrE / QrE windows per key tile
-//   9     UMMA issuer (one elected lane) and TMEM owner
-//   10    unit preparation (one unit ahead, two-slot ring)
-//   11    idle
+//   4-11  position warps: warp w reads TMEM lanes 32 (w % 4) .. + 31; warps 4-7 take the
+//         first half of each product's columns, warps 8-11 the second half
+//   12    TMA producer: Q per unit; K / V (2-stage rings), KrE / QrE windows per key tile
+//   13    UMMA issuer (one elected lane) and TMEM owner
+//   14    unit preparation (one unit ahead, two-slot ring)
+//   15    idle
 // TMEM (512 columns): S [0, 128), P (bf16 / fp16 pairs) [128, 192), O [192, 256),
 // X [256, 512) = the current position product (Pc, then P2).
 // Work units: 128 query rows of one (batch, head); pairs (batch, query block) are ordered by
@@ -54,20 +55,22 @@ constexpr int kBM = 128;                     // query rows per unit
 constexpr int kBN = 128;                     // keys per tile
 constexpr int kD = 64;                       // head dim
 constexpr int kTile = kBM * kD * 2;          // 16 KB: a 128 x 64 16-bit tile
-constexpr int kThreads = 384;
-constexpr int kPosWarp0 = 4;
-constexpr int kLoadWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kPrepWarp = 10;
+constexpr int kThreads = 512;
+constexpr int kPosWarp0 = 4;                 // position warps 4-11
+constexpr int kPosThreads = 256;
+constexpr int kLoadWarp = 12;
+constexpr int kMmaWarp = 13;
+constexpr int kPrepWarp = 14;
+constexpr int kTeardownThreads = 128 + kPosThreads + 32;   // softmax, position and MMA warps
 constexpr uint32_t kColS = 0, kColP = 128, kColO = 192, kColX = 256, kTmemCols = 512;
 constexpr int kMaxRel = 1024;                // index-table radius limit
 constexpr int kMaxLut = 2 * kMaxRel + 1;
 constexpr int kMaxTiles = 512;               // key tiles per sequence (N <= 65536)
 constexpr float kLog2e = 1.4426950408889634f;
-// Launched at 168 registers; softmax 232, position warps 136, producers 136
-// (128 * (232 + 136 + 136) = 384 * 168).
-constexpr uint32_t kRegsSoftmax = 232, kRegsPos = 136, kRegsProd = 136;
-static_assert(128 * (kRegsSoftmax + kRegsPos + kRegsProd) == 384 * 168, "setmaxnreg split must use the launch budget");
+// Launched at 128 registers; softmax 200, position warps 112, producers 88
+// (128 * (200 + 2 * 112 + 88) = 512 * 128).
+constexpr uint32_t kRegsSoftmax = 200, kRegsPos = 112, kRegsProd = 88;
+static_assert(128 * (kRegsSoftmax + 2 * kRegsPos + kRegsProd) == 512 * 128, "setmaxnreg split must use the launch budget");
 
 // Shared memory (offsets from a 1024-aligned base).
 constexpr int kOffQ = 0;                     // Q tile, 128-byte swizzle (TMA)
@@ -255,6 +258,15 @@ __device__ __forceinline__ uint32_t mnmajor_sw64(uint32_t base, int m, int k) {
   return base + (m >> 5) * 8192 + k * 64 + 16 * ((min_ >> 3) ^ ((k >> 1) & 3)) + 2 * (min_ & 7);
 }
 
+// Both staging tiles store 4-byte words (pairs of fp16 along the contiguous dimension): in
+// word units, lane row `r` (64 bytes per row) word `t` (0..63) sits at
+//   r * 64 + (t / 16) * 8192 + ((4 t mod 64) XOR 16 ((r >> 1) & 3)),
+// the two formulas above with the lane terms hoisted (lanebase = base + 64 r, x16).
+__device__ __forceinline__ uint32_t sw64_word_addr(uint32_t lanebase, uint32_t x16, int t) {
+  const uint32_t u = static_cast<uint32_t>(t);
+  return lanebase + ((u >> 4) << 13) + (((u << 2) & 60u) ^ x16);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constant__ FParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -302,17 +314,17 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
       mbar_init(&info_full[s], 32);
-      mbar_init(&info_empty[s], 128 + 128 + 1 + 1);
+      mbar_init(&info_empty[s], 128 + kPosThreads + 1 + 1);
     }
     mbar_init(kr_full, 1);
     mbar_init(kr_empty, 1);
     mbar_init(qr_full, 1);
     mbar_init(qr_empty, 1);
     mbar_init(x_full, 1);
-    mbar_init(x_empty, 128);
-    mbar_init(xc_full, 128);
+    mbar_init(x_empty, kPosThreads);
+    mbar_init(xc_full, kPosThreads);
     mbar_init(xc_empty, 1);
-    mbar_init(xp_full, 128);
+    mbar_init(xp_full, kPosThreads);
     mbar_init(xp_empty, 1);
     mbar_init(s_full, 1);
     mbar_init(s_consumed, 128);
@@ -498,18 +510,40 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
           if (nkv == 0) continue;
           if (!mbar_wait(q_full, qi & 1, abort_flag)) { ok = false; break; }
           ++qi;
+          // Pc = Q . KrE_win^T -> X, once X is free (the previous product's columns are in the
+          // position warps' registers) and the tile's KrE window has landed.
+          auto issue_pc = [&](int g) -> bool {
+            if ((prod >= 1 && !mbar_wait(x_empty, (prod - 1) & 1, abort_flag)) ||
+                !mbar_wait(kr_full, g & 1, abort_flag))
+              return false;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < kD / 16; ++kk)
+              umma_ss(tX, smem_desc(sQ + kk * 32, 16, 1024, kLayoutSw128),
+                      smem_desc(sKr + kk * 32, 16, 1024, kLayoutSw128), idesc_pos, kk > 0 ? 1u : 0u);
+            umma_commit(kr_empty);
+            umma_commit(x_full);
+            ++prod;
+            return true;
+          };
+          bool pc_ready = false;     // Pc of this tile was issued during the previous tile
           for (int t = 0; t < nkv && ok; ++t, ++G) {
             const int s = G & 1;
-            // Pc = Q . KrE_win^T -> X
-            if (p.has_c2p) {
+            if (p.has_c2p && !pc_ready && !issue_pc(G)) { ok = false; break; }
+            // P2 = K . QrE_win^T -> X first: it waits only for this tile's c2p columns to leave
+            // X, while S = Q K^T below waits for the previous tile's softmax to read S.
+            if (p.has_p2c) {
               if ((prod >= 1 && !mbar_wait(x_empty, (prod - 1) & 1, abort_flag)) ||
-                  !mbar_wait(kr_full, G & 1, abort_flag)) { ok = false; break; }
+                  !mbar_wait(qr_full, G & 1, abort_flag) || !mbar_wait(&k_full[s], (G >> 1) & 1, abort_flag)) {
+                ok = false;
+                break;
+              }
               tc_fence_after();
 #pragma unroll
               for (int kk = 0; kk < kD / 16; ++kk)
-                umma_ss(tX, smem_desc(sQ + kk * 32, 16, 1024, kLayoutSw128),
-                        smem_desc(sKr + kk * 32, 16, 1024, kLayoutSw128), idesc_pos, kk > 0 ? 1u : 0u);
-              umma_commit(kr_empty);
+                umma_ss(tX, smem_desc(sK + s * kTile + kk * 32, 16, 1024, kLayoutSw128),
+                        smem_desc(sQr + kk * 32, 16, 1024, kLayoutSw128), idesc_pos, kk > 0 ? 1u : 0u);
+              umma_commit(qr_empty);
               umma_commit(x_full);
               ++prod;
             }
@@ -522,19 +556,6 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
               umma_ss(tS, smem_desc(sQ + kk * 32, 16, 1024, kLayoutSw128),
                       smem_desc(sK + s * kTile + kk * 32, 16, 1024, kLayoutSw128), idesc_qk, kk > 0 ? 1u : 0u);
             if (t == nkv - 1) umma_commit(q_empty);
-            // P2 = K . QrE_win^T -> X
-            if (p.has_p2c) {
-              if ((prod >= 1 && !mbar_wait(x_empty, (prod - 1) & 1, abort_flag)) ||
-                  !mbar_wait(qr_full, G & 1, abort_flag)) { ok = false; break; }
-              tc_fence_after();
-#pragma unroll
-              for (int kk = 0; kk < kD / 16; ++kk)
-                umma_ss(tX, smem_desc(sK + s * kTile + kk * 32, 16, 1024, kLayoutSw128),
-                        smem_desc(sQr + kk * 32, 16, 1024, kLayoutSw128), idesc_pos, kk > 0 ? 1u : 0u);
-              umma_commit(qr_empty);
-              umma_commit(x_full);
-              ++prod;
-            }
             umma_commit(&k_empty[s]);
             // S += c2p tile, then S += p2c tile (16 columns per product, identity B)
             if (p.has_c2p) {
@@ -546,6 +567,13 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
                         id_desc, idesc_idc, 1u);
               umma_commit(xc_empty);
             }
+            // O (+)= P V of the previous tile: its P is ready by now, and the tensor cores run it
+            // while the position warps store this tile's p2c scores.
+            if (pend >= 0 && !issue_pv()) { ok = false; break; }
+            // The next tile's Pc as soon as this tile's P2 has left X (same unit): it runs while
+            // the p2c scores are being stored.
+            pc_ready = p.has_c2p && t + 1 < nkv;
+            if (pc_ready && !issue_pc(G + 1)) { ok = false; break; }
             if (p.has_p2c) {
               if (!mbar_wait(xp_full, G & 1, abort_flag)) { ok = false; break; }
               tc_fence_after();
@@ -555,8 +583,6 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
               umma_commit(xp_empty);
             }
             umma_commit(s_full);
-            // O (+)= P V of the previous tile (its P is ready while this tile's scores were formed)
-            if (pend >= 0 && !issue_pv()) { ok = false; break; }
             pend = G;
             pend_first = t == 0 ? 1 : 0;
           }
@@ -572,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
       }
       __syncwarp();
       tc_fence_before();
-      named_bar_sync(1, 288);
+      named_bar_sync(1, kTeardownThreads);
       tc_fence_after();
       tmem_dealloc(tmem, kTmemCols);
     }
@@ -582,16 +608,30 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
   if (warp >= kPosWarp0) {
     // ------------------------------------------------------------------ position warps
     reg_dealloc<kRegsPos>();
-    const int s = warp - kPosWarp0;
+    const int s = warp & 3;                       // TMEM lane quadrant
+    const int half = (warp - kPosWarp0) >> 2;     // 0: first 80 columns of a product's range, 1: the rest
     const int i = 32 * s + lane;                  // TMEM lane: query row (Pc) / key row (P2)
     const uint32_t tX = tmem + (static_cast<uint32_t>(32 * s) << 16) + kColX;
     const uint32_t sXc = smem_u32(smem + kOffXc), sXp = smem_u32(smem + kOffXp);
-    // c2p: word of slots (j0, j0 + 1) = (col c, col c - 1); even rows pair (2u+1, 2u) of a
-    // chunk, odd rows (2u, 2u-1), the latter built from the previous pair's low half.
+    // c2p: word of slots (j0, j0 + 1) = (col c, col c - 1); even rows pair (2w+1, 2w) of a
+    // 16-column group, odd rows (2w, 2w-1), the latter built from the previous pair's high
+    // column.
     const uint32_t sel_c = (i & 1) ? 0x1076u : 0x7654u;
-    // p2c: word of M-slots (i0, i0 + 1) = (col c, col c + 1); odd keys pair (2u, 2u+1), even
-    // keys (2u+1, 2u+2), built with the next pair's low half.
+    // p2c: word of M-slots (i0, i0 + 1) = (col c, col c + 1); odd keys pair (2w, 2w+1), even
+    // keys (2w+1, 2w+2), built with the next pair's low column.
     const uint32_t sel_p = (i & 1) ? 0x3210u : 0x5432u;
+    // Row i needs Pc columns [i, i + 127]: the quadrant reads [32 s, 32 s + 160), this warp its
+    // half [32 s + 80 half, + 80), plus the two columns before it (the pairing carry).  Key j
+    // needs P2 columns [127 - j, 254 - j]: the quadrant reads [96 - 32 s, 256 - 32 s), this
+    // warp its half, plus the two columns after it (the last pair's partner).
+    const int cbc = 32 * s + 80 * half;
+    const int cbp = 96 - 32 * s + 80 * half;
+    // Word addresses: the lane's row (c2p: query row i of Xc; p2c: key row i of the MN-major
+    // Xp) and swizzle term, and the word index of the lane's first pair: c2p word
+    // t = tc0 - 8 group - w (slots 2t, 2t + 1), p2c word t = tp0 + 8 group + w.
+    const uint32_t xc_lane = sXc + 64u * i, xp_lane = sXp + 64u * i, x16 = 16u * ((i >> 1) & 3);
+    const int tc0 = ((i + (i & 1)) >> 1) + 63 - (cbc >> 1);
+    const int tp0 = (cbp >> 1) + ((i + ((i + 1) & 1) - (kBN - 1)) >> 1);
     int G = 0, prod = 0;
     bool aborted = false;
     for (int ui = 0; !aborted; ++ui) {
@@ -609,27 +649,33 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
           if (G >= 1) ok = ok && mbar_wait(xc_empty, (G - 1) & 1, abort_flag);
           if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
           tc_fence_after();
-          // Row i needs columns [i, i + 127]; the warp reads [32 s, 32 s + 160) in 5 chunks.
-          uint32_t carry = 0u;
-#pragma unroll 1
-          for (int q = 0; q < 5; ++q) {
-            const int cb = 32 * s + 32 * q;
-            uint32_t R[32];
-            tmem_ld_x32(tX + cb, R);
-            if (q == 4) {
+          // 16 columns at a time; the next group's load is in flight while one is stored.
+          uint32_t A[16], B[16], E[2];
+          tmem_ld_x16_nowait(tX + cbc, A);
+          tmem_ld_x2_nowait(tX + (half ? cbc - 2 : cbc), E);
+          tmem_wait_ld_regs2(A, E);
+          uint32_t carry = half ? pack_f16x2_sat(__uint_as_float(E[1]), __uint_as_float(E[0])) : 0u;
+#pragma unroll
+          for (int hq = 0; hq < 5; ++hq) {
+            uint32_t (&cur)[16] = (hq & 1) ? B : A;
+            uint32_t (&nxt)[16] = (hq & 1) ? A : B;
+            if (hq < 4) tmem_ld_x16_nowait(tX + cbc + 16 * (hq + 1), nxt);
+            uint32_t F[8];
+#pragma unroll
+            for (int w = 0; w < 8; ++w)
+              F[w] = pack_f16x2_sat(__uint_as_float(cur[2 * w + 1]), __uint_as_float(cur[2 * w]));
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+              const uint32_t word = prmt(w == 0 ? carry : F[w - 1], F[w], sel_c);
+              const int t = tc0 - 8 * hq - w;
+              if (static_cast<unsigned>(t) <= 63u) st_shared_u32(sw64_word_addr(xc_lane, x16, t), word);
+            }
+            carry = F[7];
+            if (hq < 4) tmem_wait_ld_regs(nxt);
+            if (hq == 3) {
               tc_fence_before();
-              mbar_arrive(x_empty);
+              mbar_arrive(x_empty);               // every column of this product is in registers
             }
-            uint32_t F[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) F[u] = pack_f16x2_sat(__uint_as_float(R[2 * u + 1]), __uint_as_float(R[2 * u]));
-#pragma unroll
-            for (int u = 0; u < 16; ++u) {
-              const uint32_t w = prmt(u == 0 ? carry : F[u - 1], F[u], sel_c);
-              const int j0 = i - cb - 2 * u + 126 + (i & 1);
-              if (j0 >= 0 && j0 <= 126) st_shared_u32(kmajor_sw64(sXc, i, j0), w);
-            }
-            carry = F[15];
           }
           fence_proxy_async_smem();
           mbar_arrive(xc_full);
@@ -640,32 +686,39 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
           if (G >= 1) ok = ok && mbar_wait(xp_empty, (G - 1) & 1, abort_flag);
           if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
           tc_fence_after();
-          // Key j needs columns [127 - j, 254 - j]; the warp reads [96 - 32 s, 256 - 32 s).
-          uint32_t prev15 = 0u;
-#pragma unroll 1
-          for (int q = 0; q < 5; ++q) {
-            const int cb = 96 - 32 * s + 32 * q;
-            uint32_t R[32];
-            tmem_ld_x32(tX + cb, R);
-            if (q == 4) {
+          // Each 16-column group is loaded with the two columns after it (its last pair's
+          // partner), so no wait falls inside a group; the last group of the second half has
+          // no partner it needs.
+          uint32_t A[16], B[16], EA[2], EB[2];
+          tmem_ld_x16_x2_nowait(tX + cbp, tX + cbp + 16, A, EA);
+          tmem_wait_ld_regs2(A, EA);
+#pragma unroll
+          for (int hq = 0; hq < 5; ++hq) {
+            uint32_t (&cur)[16] = (hq & 1) ? B : A;
+            uint32_t (&nxt)[16] = (hq & 1) ? A : B;
+            uint32_t (&ecur)[2] = (hq & 1) ? EB : EA;
+            uint32_t (&enxt)[2] = (hq & 1) ? EA : EB;
+            // (the second half's last group has no partner: its extra load re-reads the group
+            // start, since the columns after it lie past the product)
+            if (hq < 4)
+              tmem_ld_x16_x2_nowait(tX + cbp + 16 * (hq + 1),
+                                    tX + cbp + 16 * (hq + 1) + ((hq == 3 && half) ? 0 : 16), nxt, enxt);
+            uint32_t Gp[9];
+#pragma unroll
+            for (int w = 0; w < 8; ++w)
+              Gp[w] = pack_f16x2_sat(__uint_as_float(cur[2 * w]), __uint_as_float(cur[2 * w + 1]));
+            Gp[8] = (hq == 4 && half) ? 0u : pack_f16x2_sat(__uint_as_float(ecur[0]), __uint_as_float(ecur[1]));
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+              const uint32_t word = prmt(Gp[w], Gp[w + 1], sel_p);
+              const int t = tp0 + 8 * hq + w;
+              if (static_cast<unsigned>(t) <= 63u) st_shared_u32(sw64_word_addr(xp_lane, x16, t), word);
+            }
+            if (hq < 4) tmem_wait_ld_regs2(nxt, enxt);
+            if (hq == 3) {
               tc_fence_before();
-              mbar_arrive(x_empty);
+              mbar_arrive(x_empty);               // the last group is in registers
             }
-            uint32_t Gp[16];
-#pragma unroll
-            for (int u = 0; u < 16; ++u) Gp[u] = pack_f16x2_sat(__uint_as_float(R[2 * u]), __uint_as_float(R[2 * u + 1]));
-            if (q > 0) {   // the previous chunk's last pair, which needed this chunk's first value
-              const uint32_t w = prmt(prev15, Gp[0], sel_p);
-              const int i0 = (cb - 32) + 30 + ((i + 1) & 1) + i - (kBN - 1);
-              if (i0 >= 0 && i0 <= 126) st_shared_u32(mnmajor_sw64(sXp, i0, i), w);
-            }
-#pragma unroll
-            for (int u = 0; u < 15; ++u) {
-              const uint32_t w = prmt(Gp[u], Gp[u + 1], sel_p);
-              const int i0 = cb + 2 * u + ((i + 1) & 1) + i - (kBN - 1);
-              if (i0 >= 0 && i0 <= 126) st_shared_u32(mnmajor_sw64(sXp, i0, i), w);
-            }
-            prev15 = Gp[15];
           }
           fence_proxy_async_smem();
           mbar_arrive(xp_full);
@@ -674,7 +727,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
       }
     }
     tc_fence_before();
-    named_bar_sync(1, 288);
+    named_bar_sync(1, kTeardownThreads);
     return;
   }
 
@@ -883,7 +936,7 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
   // This thread's output stores have landed (tile stores: row 0; packed rows: every thread).
   if (p.cu_seqlens != nullptr || threadIdx.x == 0) bulk_wait_all();
   tc_fence_before();
-  named_bar_sync(1, 288);
+  named_bar_sync(1, kTeardownThreads);
 }
 
 // Error word of this file (vf_device_error gathers it).

@@ -15,9 +15,12 @@ stacks measure encoder tokens/s with the hot path in place:
                     tanh GELU through this package's fused_gelu_mul_dropout as at :418,
                     final RMS norm).
 
-Position scores for DeBERTa are formed per packed row: pos_key[t, h, :] = q[t, h] . Kr[:, h]
-and pos_query[t, h, :] = k[t, h] . Qr[:, h] (Kr = key_proj(rel), Qr = query_proj(rel),
-biases included), then handed to the op as [T, H, 2S] views without a copy.
+DeBERTa's position terms: by default the stack passes Kr = key_proj(rel) and
+Qr = query_proj(rel) (biases included) to the op's fused mode, which forms q . Kr and
+k . Qr on the tensor cores inside the attention kernel.  With `fused_positions=False` it
+forms them as the reference's caller does, per packed row (pos_key[t, h, :] = q[t, h] . Kr,
+pos_query[t, h, :] = k[t, h] . Qr, two batched GEMMs), and hands them over as [T, H, 2S]
+views.
 """
 from __future__ import annotations
 
@@ -90,7 +93,7 @@ class DebertaV3Encoder:
     any function of the same signature, e.g. a CPU oracle)."""
 
     def __init__(self, cfg: DebertaConfig = DebertaConfig(), device="cuda", dtype=torch.bfloat16, seed: int = 0,
-                 attention_fn=None, add_norm=None, act_fn=None):
+                 attention_fn=None, add_norm=None, act_fn=None, fused_positions: bool = True):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         g = torch.Generator(device=self.device).manual_seed(seed)
         E, F_, S2 = cfg.hidden, cfg.ffn, 2 * cfg.position_buckets
@@ -118,6 +121,7 @@ class DebertaV3Encoder:
         # torch's exact GELU (the reference's ACT2FN["gelu"]); exact_gelu_kernel, this
         # package's activation-only kernel, measured the same C3 tokens/s in its place
         self.act_fn = F.gelu if act_fn is None else act_fn
+        self.fused_positions = fused_positions
 
     @torch.no_grad()
     def forward(self, ids: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
@@ -132,10 +136,16 @@ class DebertaV3Encoder:
             # share_att_key: Kr = key_proj(rel), Qr = query_proj(rel), biases included
             rq = torch.addmm(L["bqkv"][:E], rel, L["wqkv"][:E].t()).view(-1, H, D)
             rk = torch.addmm(L["bqkv"][E:2 * E], rel, L["wqkv"][E:2 * E].t()).view(-1, H, D)
-            pos_key = torch.bmm(q.transpose(0, 1), rk.permute(1, 2, 0)).transpose(0, 1)     # [T, H, 2S]
-            pos_query = torch.bmm(k.transpose(0, 1), rq.permute(1, 2, 0)).transpose(0, 1)
-            ctx = self.attention_fn(q, k, v, cu_seqlens, max_seqlen, pos_key, pos_query, False, sm_scale,
-                                    cfg.position_buckets, cfg.max_relative_positions, True)
+            if self.fused_positions:
+                # (H, 2S, D) views of the projections; the kernel forms q . Kr and k . Qr
+                ctx = self.attention_fn(q, k, v, cu_seqlens, max_seqlen, None, None, False, sm_scale,
+                                        cfg.position_buckets, cfg.max_relative_positions, True,
+                                        rel_key=rk.permute(1, 0, 2), rel_query=rq.permute(1, 0, 2))
+            else:
+                pos_key = torch.bmm(q.transpose(0, 1), rk.permute(1, 2, 0)).transpose(0, 1)     # [T, H, 2S]
+                pos_query = torch.bmm(k.transpose(0, 1), rq.permute(1, 2, 0)).transpose(0, 1)
+                ctx = self.attention_fn(q, k, v, cu_seqlens, max_seqlen, pos_key, pos_query, False, sm_scale,
+                                        cfg.position_buckets, cfg.max_relative_positions, True)
             a = torch.addmm(L["bo"], ctx.reshape(T, E).to(h.dtype), L["wo"].t())
             h = self.add_norm(a, h, *L["ln1"], cfg.eps)
             f = self.act_fn(torch.addmm(L["b1"], h, L["w1"].t()))
@@ -147,8 +157,9 @@ class DebertaV3Encoder:
         return self.cfg.layers * 2.0 * (4 * E * E + 2 * E * F_)
 
     def own_launches_per_layer(self) -> int:
-        """This package's kernel launches per layer: the attention and two add + LayerNorm."""
-        return 3
+        """This package's kernel launches per layer: the attention (with the fused mode's
+        set-up kernel) and two add + LayerNorm."""
+        return 4 if self.fused_positions else 3
 
 
 class MT5Encoder:

@@ -150,7 +150,8 @@ def deberta_varlen_inputs(seed: int = 0, device="cuda", B: int = 8, L: int = 512
     cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(lens), 0).tolist()), dtype=torch.int32)
     out = {k: w[k] for k in ("lengths", "sm_scale", "position_buckets", "max_relative_distance", "use_log_bucket")}
     out.update(q=pack(w["q"]), k=pack(w["k"]), v=pack(w["v"]), pos_key=pack(w["pos_key"]),
-               pos_query=pack(w["pos_query"]), cu_seqlens=cu.to(w["q"].device), max_seqlen=max(lens))
+               pos_query=pack(w["pos_query"]), cu_seqlens=cu.to(w["q"].device), max_seqlen=max(lens),
+               rel_key=w["rel_key"], rel_query=w["rel_query"])
     return out
 
 
