@@ -192,6 +192,23 @@ int vf_deberta_attention_fused_varlen_fwd(const vf_deberta_fused_args_t* args, c
                                           int32_t num_seqs, int32_t max_seqlen, void* workspace,
                                           int64_t workspace_bytes, void* stream);
 
+/* The fused operator for callers that cannot allocate device memory per call; it has no
+ * counterpart in the reference.  An FFI host (cgo, JNI, ctypes) that embeds this library
+ * without a CUDA allocator of its own, or a serving process whose device memory is reserved
+ * up front by its own pool (the KV-cache reservation of a vLLM-style engine), may have no
+ * way to provide the workspace of vf_deberta_attention_fused_fwd.  This entry point takes
+ * the same arguments minus the workspace and uses a fixed 8 MiB scratch array compiled into
+ * the library instead (held by every GPU that loads the library, until the process exits).
+ * It calls no cudaMalloc, cudaFree or allocating library routine.
+ * Limit: the call's scratch, vf_deberta_fused_workspace_bytes(B, H, M, N), must be at most
+ * 8 MiB (for example H = 16 with ceil128(M) + ceil128(N) <= 2048); larger calls return
+ * VF_EUNSUPPORTED before any launch.
+ * The first call on a device looks up the scratch array's device address (once per device,
+ * with that device current); make that first call before any stream capture.  Every call
+ * shares the one array, so calls that overlap on the GPU (other streams, other host
+ * threads) race; nothing in it needs to start at zero, each call rewrites what it reads. */
+int vf_deberta_attention_fused_noalloc_fwd(const vf_deberta_fused_args_t* args, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * Gated activation of the mT5 feed-forward: out = act(gate) * up, in fp32, rounded to the
  * dtype.  Replaces kernels/ff_fused.py:86 `fused_gelu_mul_dropout(gate, up, act_fn,

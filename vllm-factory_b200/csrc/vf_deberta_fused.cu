@@ -939,6 +939,14 @@ __global__ void __launch_bounds__(kThreads, 1) fused_kernel(const __grid_constan
   named_bar_sync(1, kTeardownThreads);
 }
 
+// Scratch of vf_deberta_attention_fused_noalloc_fwd: the expanded position tables and the
+// unit order live here instead of in a caller-provided workspace.  Every GPU that loads the
+// library holds these 8 MiB until the process exits.  In host code the name is only a
+// host-side stand-in for the device array; its device address comes from
+// cudaGetSymbolAddress (noalloc_scratch below).
+constexpr long long kNoAllocScratchBytes = 8LL << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
 // Error word of this file (vf_device_error gathers it).
 }  // namespace dfz
 
@@ -1129,9 +1137,50 @@ int fused_run(const vf_deberta_fused_args_t* a, long long batch, long long M, lo
                                    : launch_fused<__half>(fp, pp, units, chunks, stream);
 }
 
+// Device address of the static scratch array on the current device, looked up once per device
+// (with that device current) and cached.  Returns nullptr and sets the error message when the
+// lookup fails.
+void* noalloc_scratch() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    fail(VF_ECUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+    return nullptr;
+  }
+  static std::once_flag flags[64];
+  static void* ptr[64];
+  static cudaError_t err[64];
+  if (dev < 0 || dev >= 64) {
+    fail(VF_ECUDA, "device ordinal out of range");
+    return nullptr;
+  }
+  std::call_once(flags[dev], [&] { err[dev] = cudaGetSymbolAddress(&ptr[dev], vf::dfz::g_noalloc_scratch); });
+  if (err[dev] != cudaSuccess || ptr[dev] == nullptr) {
+    fail(VF_ECUDA, std::string("cudaGetSymbolAddress of the static scratch: ") + cudaGetErrorString(err[dev]));
+    return nullptr;
+  }
+  return ptr[dev];
+}
+
 }  // namespace
 
 extern "C" {
+
+int vf_deberta_attention_fused_noalloc_fwd(const vf_deberta_fused_args_t* a, void* stream) {
+  if (a == nullptr) return fail(VF_EINVAL, "null args");
+  int rc = vf::host_check_qkv(a->q, a->k, a->v, a->out);
+  if (rc) return rc;
+  const long long need = geometry(a->q.size[0], a->q.size[1], a->q.size[2], a->k.size[2]).total;
+  if (need > vf::dfz::kNoAllocScratchBytes)
+    return fail(VF_EUNSUPPORTED, "deberta fused noalloc: this call needs " + std::to_string(need) +
+                                     " bytes of scratch; the static scratch holds " +
+                                     std::to_string(vf::dfz::kNoAllocScratchBytes) +
+                                     " (use vf_deberta_attention_fused_fwd with a workspace)");
+  void* scratch = noalloc_scratch();
+  if (scratch == nullptr) return VF_ECUDA;
+  return fused_run(a, a->q.size[0], a->q.size[2], a->k.size[2], nullptr, 0, scratch, vf::dfz::kNoAllocScratchBytes,
+                   static_cast<cudaStream_t>(stream));
+}
 
 int64_t vf_deberta_fused_workspace_bytes(int64_t batch_or_seqs, int64_t heads, int64_t M, int64_t N) {
   if (batch_or_seqs < 0 || heads < 0 || M < 0 || N < 0) return fail(VF_EINVAL, "negative size");

@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "vf_deberta_attention_fused_fwd",
     "vf_deberta_attention_fused_varlen_fwd",
     "vf_deberta_fused_workspace_bytes",
+    "vf_deberta_attention_fused_noalloc_fwd",
     "vf_gated_act_fwd",
     "vf_add_layer_norm_fwd",
     "vf_t5_relative_bucket",
@@ -193,6 +194,8 @@ def load() -> ctypes.CDLL:
                                                               ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
                                                               ctypes.c_int64, ctypes.c_void_p]
         lib.vf_deberta_attention_fused_varlen_fwd.restype = ctypes.c_int
+        lib.vf_deberta_attention_fused_noalloc_fwd.argtypes = [ctypes.POINTER(DebertaFusedArgs), ctypes.c_void_p]
+        lib.vf_deberta_attention_fused_noalloc_fwd.restype = ctypes.c_int
         lib.vf_gated_act_fwd.argtypes = [ctypes.POINTER(GatedActArgs), ctypes.c_void_p]
         lib.vf_gated_act_fwd.restype = ctypes.c_int
         lib.vf_add_layer_norm_fwd.argtypes = [ctypes.POINTER(AddLayerNormArgs), ctypes.c_void_p]
