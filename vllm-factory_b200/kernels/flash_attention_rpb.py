@@ -17,6 +17,8 @@ import torch
 
 import vf_b200.ops  # noqa: F401  (loads the kernels and registers torch.ops.vf_b200)
 
+from . import varlen_glue
+
 
 def flash_attention_rpb_final(
     q: torch.Tensor,
@@ -33,8 +35,18 @@ def flash_attention_rpb_final(
 ) -> torch.Tensor:
     """Same arguments and result as the reference.  `use_autotune` is accepted and ignored:
     the kernel has a single tile configuration.  `dropout_p` must be 0 (inference path;
-    the reference's callers always pass 0)."""
+    the reference's callers always pass 0).  Inside `varlen_glue.packed_batch`, a flat call
+    (q of shape (1, H, T, 64) over the batch's T tokens) runs as the batch's requests, each
+    attending only within itself; the flat call's padding mask (all zero) is not read."""
     del use_autotune
+    batch = varlen_glue.routes(q)
+    if batch is not None:
+        if dropout_p != 0.0:
+            raise ValueError("flash_attention_rpb_final: dropout_p must be 0 (inference path)")
+        rows = varlen_glue.packed_rows
+        return varlen_glue.flat_result(flash_attention_rpb_varlen(
+            rows(q), rows(k), rows(v), batch.cu_seqlens, batch.max_seqlen, rpb_table, num_buckets, max_distance,
+            is_decoder, softmax_scale))
     return torch.ops.vf_b200.rpb_attention(
         q, k, v, rpb_table, int(num_buckets), int(max_distance), bool(is_decoder),
         padding_mask, float(dropout_p), float(softmax_scale))

@@ -28,6 +28,8 @@ import torch
 
 import vf_b200.ops  # noqa: F401  (loads the kernels and registers torch.ops.vf_b200)
 
+from . import varlen_glue
+
 HAS_TRITON = True
 HAS_FUSED_POSITIONS = True
 
@@ -58,7 +60,16 @@ def flash_deberta_attention(
     rel_query: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """Same arguments and result as the reference (output rows past seq_len are zero).
-    With `rel_key` / `rel_query` the position products are formed inside the kernel."""
+    With `rel_key` / `rel_query` the position products are formed inside the kernel.
+    Inside `varlen_glue.packed_batch`, a flat call (q of shape (1, H, T, 64) over the
+    batch's T tokens) runs as the batch's requests, each attending only within itself."""
+    batch = varlen_glue.routes(q)
+    if batch is not None:
+        rows = varlen_glue.packed_rows
+        return varlen_glue.flat_result(flash_deberta_attention_varlen(
+            rows(q), rows(k), rows(v), batch.cu_seqlens, batch.max_seqlen, rows(pos_key), rows(pos_query),
+            causal, sm_scale, position_buckets, max_relative_distance, use_log_bucket,
+            rel_key=rel_key, rel_query=rel_query))
     if _fused_args(pos_key, pos_query, rel_key, rel_query):
         return torch.ops.vf_b200.deberta_attention_fused(
             q, k, v, seq_lengths, rel_key, rel_query, bool(causal),
