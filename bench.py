@@ -25,7 +25,8 @@ batch with the same valid lengths as rank 0's (weak scaling); the encoder stack 
 256-sequence batch over the ranks by LPT on estimated FLOPs (strong scaling).  NCCL carries
 only the barrier and the max-time / summed-work reductions.  `--impl reference` times the
 reference's CPU implementation (the oracle port) on rank 0 and prints the same metric with
-the same `config`.
+the same `config`.  `--impl reference_triton` times the reference's own Triton kernels on
+one GPU on the same input sets (a secondary bar beside the CPU reference arm).
 
 Named workloads (`--workload`): mt5_c2, mt5_c2_varlen, deberta_c1[_fused], deberta_c1_fp32,
 deberta_c1_varlen[_fused], deberta_c5_<L>[_fused] (L = 1024, 2048, 4096), the encoder
@@ -618,11 +619,69 @@ def run_add_layer_norm(args, world: int, rank: int, dev, warmup: int):
 
 
 # ----------------------------------------------------------------------------- attention lines
-def run_attention(args, name: str, steps: int, world: int, rank: int, dev, warmup: int, cpu_base: bool):
+def reference_triton_kernels():
+    """The reference's own Triton modules (kernels/flash_attention_rpb.py,
+    kernels/flash_deberta_attention.py) from the reference install (VF_REFERENCE, else
+    baseline/_ref), loaded under private names so they never shadow this repository's
+    `kernels` package.  Returns (modules, None) or (None, why)."""
+    import importlib.util
+    ref = Path(os.environ.get("VF_REFERENCE", str(ROOT / "baseline" / "_ref")))
+    mods = {}
+    for m in ("flash_attention_rpb", "flash_deberta_attention"):
+        path = ref / "kernels" / f"{m}.py"
+        if not path.exists():
+            return None, f"no reference install at {ref}"
+        spec = importlib.util.spec_from_file_location(f"_vf_reference_triton_{m}", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        mods[m] = mod
+    if not getattr(mods["flash_deberta_attention"], "HAS_TRITON", False):
+        return None, "the reference's Triton kernels did not import"
+    return mods, None
+
+
+def reference_triton_call(name: str, mods: dict):
+    """The reference's stock GPU path for a workload, on the same input sets as this
+    repository's arm: flash_attention_rpb_final as T5SelfAttention.forward calls it
+    (models/mt5/mt5_encoder.py:269-280), and flash_deberta_attention with the caller's
+    position products as DisentangledSelfAttentionV2._flash_forward forms them
+    (models/deberta_v2/deberta_v2_encoder.py:275-322).  For a fused workload every step also
+    forms those products (torch matmuls), which is the work the fused kernel absorbs."""
+    if "varlen" in name:
+        return None
+    if name == "mt5_c2":
+        fn = mods["flash_attention_rpb"].flash_attention_rpb_final
+        return lambda x: fn(x["q"], x["k"], x["v"], rpb_table=x["rpb_table"], num_buckets=32, max_distance=128,
+                            is_decoder=False, padding_mask=x["padding_mask"], dropout_p=0.0, softmax_scale=1.0,
+                            use_autotune=True)
+    fn = mods["flash_deberta_attention"].flash_deberta_attention
+    if name.endswith("_fused"):
+        def call(x):
+            pk = torch.matmul(x["q"], x["rel_key"].transpose(-1, -2))
+            pq = torch.matmul(x["k"], x["rel_query"].transpose(-1, -2).to(dtype=x["k"].dtype))
+            return fn(q=x["q"], k=x["k"], v=x["v"], seq_lengths=x["seq_lengths"], pos_key=pk, pos_query=pq,
+                      causal=False, sm_scale=x["sm_scale"], position_buckets=256, max_relative_distance=512,
+                      use_log_bucket=True)
+        return call
+    return lambda x: fn(q=x["q"], k=x["k"], v=x["v"], seq_lengths=x["seq_lengths"], pos_key=x["pos_key"],
+                        pos_query=x["pos_query"], causal=False, sm_scale=x["sm_scale"], position_buckets=256,
+                        max_relative_distance=512, use_log_bucket=True)
+
+
+def run_attention(args, name: str, steps: int, world: int, rank: int, dev, warmup: int, cpu_base: bool,
+                  impl: str = "ours"):
     """One attention workload: `steps` calls of the drop-in, each on a different input set,
     timed on the device; value = valid FLOPs of all ranks / max rank time.  Every rank takes
-    the same collective steps; rank 0 gets the line, the others None."""
+    the same collective steps; rank 0 gets the line, the others None.  impl="reference_triton"
+    times the reference's Triton path (reference_triton_call) on the same inputs, without the
+    e2e and CPU legs."""
     sets, call, flops, tokens, cfg, keys, lens, launches = build_workload(name, rank, dev)
+    if impl == "reference_triton":
+        mods, why = reference_triton_kernels()
+        call = reference_triton_call(name, mods) if mods else None
+        if call is None:
+            return {"impl": impl, "unavailable": why or f"the reference has no GPU path for {name}"}
+        launches, cpu_base = None, False
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -654,7 +713,7 @@ def run_attention(args, name: str, steps: int, world: int, rank: int, dev, warmu
 
     # ---- end to end through the public call, host buffers, copies inside the timed region
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and impl == "ours":
         host = {k: (v.cpu().pin_memory() if isinstance(v, torch.Tensor) and v.is_cuda and k in keys else v)
                 for k, v in sets[0].items()}
         n_e2e = max(3, min(steps, 30))
@@ -680,7 +739,11 @@ def run_attention(args, name: str, steps: int, world: int, rank: int, dev, warmu
             "vs_baseline": None, "dtype": dtype_label, "data": "synthetic", "config": cfg, "l2": l2_note,
             "tokens_per_s": tokens_all * steps / (ms_max * 1e-3),
             "pct_bf16_peak": value / (peaks["bf16"] * world),
-            "roofline": roofline, "gpu_launches": steps * launches, "clocks": clocks, "e2e": e2e}
+            "roofline": roofline, "gpu_launches": steps * launches if launches else None, "clocks": clocks,
+            "e2e": e2e}
+    if impl != "ours":
+        line["impl"] = impl
+        line["roofline"]["traffic"] = None
     if world == 1 and cpu_base:
         line["cpu_baseline"] = cpu_baseline(name, lens)
     return line
@@ -717,7 +780,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "reference_triton"],
+                    help="reference = the reference's CPU path (the oracle port) on the host cores; "
+                         "reference_triton = the reference's own Triton kernels on this GPU (one GPU, "
+                         "attention workloads; a secondary bar, not the driver's reference arm)")
     ap.add_argument("--workload", default="default",
                     help="default = mt5_c2 headline with the DeBERTa C1 attention and C3 encoder lines "
                          "as sub-results; or one of the named workloads")
@@ -747,6 +813,18 @@ def main():
         raise SystemExit("bench.py needs a CUDA GPU")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.impl == "reference_triton":
+        if rank != 0:
+            return
+        import vf_b200
+        vf_b200.load()                  # the input generators share this repository's workloads
+        line = run_attention(args, headline, args.steps, 1, 0, dev, warmup, False, impl="reference_triton")
+        if subs:
+            line["sub_results"] = {
+                w: run_attention(args, w, args.steps, 1, 0, dev, warmup, False, impl="reference_triton")
+                for w in ("deberta_c1", "deberta_c1_fused")}
+        print(json.dumps(line))
+        return
     if world > 1:
         import datetime
         # NCCL's initialisation log (communicator ranks) goes to stderr; rank 0's stdout

@@ -178,14 +178,18 @@ __device__ __forceinline__ int unit_tiles(int q0, int klen, int qlen, int causal
 }
 
 // ------------------------------------------------------------------------------ set-up kernel
-// Block 0 orders the (batch, query block) pairs by key-tile count (counting sort, longest
-// first; the order inside one count is arbitrary and only affects scheduling).  The other
-// blocks fill the expanded position tables, one 16-byte chunk per thread and step:
+// Block (0, 0) orders the (batch, query block) pairs by key-tile count (counting sort,
+// longest first; the order inside one count is arbitrary and only affects scheduling).
+// Blocks (x >= 1, y) fill the expanded position table y / H of head y % H, one 16-byte chunk
+// per thread and step (no integer division on the way):
 //   KrE[h][e][:] = rel_key[h][idx(e - e0)][:],  QrE likewise.
 __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ PrepParams p) {
   if (blockIdx.x == 0) {
+    if (blockIdx.y != 0) return;
     __shared__ int hist[kMaxTiles + 2];
+    __shared__ int top;
     for (int c = threadIdx.x; c < kMaxTiles + 2; c += blockDim.x) hist[c] = 0;
+    if (threadIdx.x == 0) top = 0;
     __syncthreads();
     const int P = p.B * p.nqb;
     for (int pi = threadIdx.x; pi < P; pi += blockDim.x) {
@@ -193,11 +197,12 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ PrepP
       seq_geometry(p.seq_lengths, p.cu_seqlens, p.packed_rows, p.M, p.N, pi / p.nqb, klen, qlen, row0);
       const int c = min(unit_tiles((pi % p.nqb) * kBM, klen, qlen, p.causal, p.p_seq), kMaxTiles);
       atomicAdd(&hist[c], 1);
+      atomicMax(&top, c);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
       int run = 0;   // exclusive start of each count, counts in decreasing order
-      for (int c = kMaxTiles; c >= 0; --c) {
+      for (int c = top; c >= 0; --c) {
         const int n = hist[c];
         hist[c] = run;
         run += n;
@@ -212,22 +217,21 @@ __global__ void __launch_bounds__(256) prep_kernel(const __grid_constant__ PrepP
     }
     return;
   }
-  const long long per_table = static_cast<long long>(p.H) * p.NE * (kD / 8);
-  const long long total = 2 * per_table;
-  const long long stride = static_cast<long long>(gridDim.x - 1) * blockDim.x;
-  for (long long g = static_cast<long long>(blockIdx.x - 1) * blockDim.x + threadIdx.x; g < total; g += stride) {
-    const int table = g >= per_table ? 1 : 0;
-    const long long rem = g - table * per_table;
-    const int chunk = static_cast<int>(rem % (kD / 8));
-    const long long row = rem / (kD / 8);
-    const int e = static_cast<int>(row % p.NE);
-    const int h = static_cast<int>(row / p.NE);
+  const int table = blockIdx.y >= static_cast<unsigned>(p.H) ? 1 : 0;
+  const int h = blockIdx.y - table * p.H;
+  const uint16_t* src_h = table ? reinterpret_cast<const uint16_t*>(p.rel_query) + h * p.rq_sh
+                                : reinterpret_cast<const uint16_t*>(p.rel_key) + h * p.rk_sh;
+  const long long ss = table ? p.rq_ss : p.rk_ss;
+  uint16_t* dst_h = reinterpret_cast<uint16_t*>(table ? p.qre : p.kre) + static_cast<long long>(h) * p.NE * kD;
+  const int per_head = p.NE * (kD / 8);
+  const int stride = (gridDim.x - 1) * blockDim.x;
+  for (int g = (blockIdx.x - 1) * blockDim.x + threadIdx.x; g < per_head; g += stride) {
+    const int chunk = g & (kD / 8 - 1);
+    const int e = g >> 3;
     const int r = min(max(e - p.e0, -p.R), p.R);
     const int idx = p.lut[r + p.R];
-    const uint16_t* src = table ? reinterpret_cast<const uint16_t*>(p.rel_query) + h * p.rq_sh + idx * p.rq_ss
-                                : reinterpret_cast<const uint16_t*>(p.rel_key) + h * p.rk_sh + idx * p.rk_ss;
-    uint16_t* dst = reinterpret_cast<uint16_t*>(table ? p.qre : p.kre) + row * kD;
-    reinterpret_cast<uint4*>(dst)[chunk] = __ldg(reinterpret_cast<const uint4*>(src) + chunk);
+    reinterpret_cast<uint4*>(dst_h + static_cast<long long>(e) * kD)[chunk] =
+        __ldg(reinterpret_cast<const uint4*>(src_h + idx * ss) + chunk);
   }
 }
 
@@ -1025,8 +1029,11 @@ int launch_fused(const vf::dfz::FParams& fp, const vf::dfz::PrepParams& pp, long
   });
   if (attr_err[dev] != cudaSuccess) return fail(VF_ECUDA, std::string("kernel set-up: ") + cudaGetErrorString(attr_err[dev]));
   const int sms = std::max(sm_count[dev], 1);
-  const long long prep_blocks = 1 + std::min<long long>((chunks + 255) / 256, 4LL * sms);
-  vf::dfz::prep_kernel<<<static_cast<unsigned>(prep_blocks), 256, 0, stream>>>(pp);
+  // x = 0: the unit order (block (0, 0)); x >= 1: the table rows of head y % H, table y / H.
+  const long long per_head = pp.H > 0 ? chunks / (2LL * pp.H) : 0;
+  const dim3 prep_grid(static_cast<unsigned>(1 + std::min<long long>((per_head + 255) / 256, 64)),
+                       static_cast<unsigned>(std::max(1, 2 * pp.H)));
+  vf::dfz::prep_kernel<<<prep_grid, 256, 0, stream>>>(pp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(VF_ECUDA, std::string("set-up kernel launch: ") + cudaGetErrorString(e));
   if (units == 0) return VF_OK;
