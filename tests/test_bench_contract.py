@@ -40,7 +40,8 @@ def test_reference_arm_other_ranks_print_nothing():
 
 def test_traffic_entries_for_captured_workloads():
     t = json.loads((ROOT / "profiles" / "traffic.json").read_text())
-    for w in ("mt5_c2", "deberta_c1", "mt5_c2_varlen", "deberta_c1_varlen", "mt5_ffn_act", "deberta_add_ln"):
+    for w in ("mt5_c2", "deberta_c1", "mt5_c2_varlen", "deberta_c1_varlen", "deberta_c1_fused", "mt5_ffn_act",
+              "deberta_add_ln"):
         assert isinstance(t.get(w), int) and t[w] > 0, w
 
 
