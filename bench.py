@@ -30,8 +30,9 @@ one GPU on the same input sets (a secondary bar beside the CPU reference arm).
 
 Named workloads (`--workload`): mt5_c2, mt5_c2_varlen, deberta_c1[_fused], deberta_c1_fp32,
 deberta_c1_varlen[_fused], deberta_c5_<L>[_fused] (L = 1024, 2048, 4096), the encoder
-stacks deberta_c3 / mt5_c4, and the HBM-bound ops beside the path, mt5_ffn_act /
-deberta_add_ln (value = GB/s).
+stacks deberta_c3 / mt5_c4, the HBM-bound ops beside the path, mt5_ffn_act /
+deberta_add_ln (value = GB/s), and the GLiNER span head downstream of the encoder,
+gliner_span (value = spans/s).
 """
 from __future__ import annotations
 
@@ -618,6 +619,127 @@ def run_add_layer_norm(args, world: int, rank: int, dev, warmup: int):
     return _run_hbm_op(args, world, rank, dev, warmup, sets, call, 3 * T * E * 2, cfg, add_layer_norm_cpu_baseline)
 
 
+# ----------------------------------------------------------------------------- GLiNER span head
+def _span_weights(m) -> dict:
+    w = {}
+    for pre, seq in (("start", m.project_start), ("end", m.project_end), ("out", m.out_project)):
+        w[f"{pre}_w1"], w[f"{pre}_b1"] = seq[0].weight.detach(), seq[0].bias.detach()
+        w[f"{pre}_w2"], w[f"{pre}_b2"] = seq[3].weight.detach(), seq[3].bias.detach()
+    return w
+
+
+GLINER_SPAN_CONFIG = {
+    "workload": "GLiNER span head (poolers/gliner.py SpanMarkerV0 + class einsum), hidden 1024, max_width 12",
+    "requests": 64, "words": "U[32,384] per request", "classes": "U[3,25] per request",
+    "weights": "N(0, 0.02), bf16", "scores": "fp32"}
+
+
+def gliner_span_cpu_baseline(budget_s: float = 12.0):
+    """The reference's span head in its own order of operations (oracle.span_scores_ref:
+    SpanMarkerV0 MLPs over words and spans, then the class einsum; fp32 torch) on the host
+    cores, one request at a time as the reference's pooler loops, for ~12 s: spans/s."""
+    import oracle
+    from vf_b200 import workloads as W
+    torch.set_num_threads(os.cpu_count() or 1)
+    b = W.gliner_span_batch(device="cpu")
+    w = {k: v.float() for k, v in _span_weights(W.gliner_span_marker(device="cpu")).items()}
+    wo, so, co = b["word_offsets"], b["span_offsets"], b["class_offsets"]
+    n_spans, g, t0 = 0, 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s and g < len(wo) - 1:
+        oracle.span_scores_ref(b["words"][wo[g]:wo[g + 1]].float()[None], b["span_idx"][so[g]:so[g + 1]][None], w,
+                               b["classes"][co[g]:co[g + 1]].float()[None], W.SPAN_MAX_WIDTH, dtype=torch.float32)
+        n_spans += so[g + 1] - so[g]
+        g += 1
+    dt = time.perf_counter() - t0
+    return {"value": n_spans / dt, "unit": "spans/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{g} of the 64 requests, one at a time, fp32 torch on CPU (oracle of the reference's "
+                      f"SpanMarkerV0 + einsum)"}
+
+
+def run_gliner_span(args, world: int, rank: int, dev, warmup: int):
+    """gliner_span: the span-scoring head of a GLiNER-large pooler over one vLLM batch of 64
+    requests (kernels.span_scores.span_scores_packed: the per-word / per-class GEMMs in torch
+    and one span-score launch).  value = spans scored per second (whole job); every rank scores
+    the same batches (weak scaling).  The roofline line is the span-score kernel alone, timed
+    on the same batches' precomputed factors."""
+    from kernels.span_scores import span_factors, span_scores_packed
+    from vf_b200 import workloads as W
+    marker = W.gliner_span_marker(device=dev)
+    sets = [W.gliner_span_batch(seed=6100 + i, device=dev) for i in range(4)]
+    offs = ("word_offsets", "span_offsets", "class_offsets")
+
+    def call(b):
+        return span_scores_packed(marker, b["words"], b["span_idx"], b["classes"], *(b[k] for k in offs),
+                                  torch.float32)
+
+    stream = torch.cuda.current_stream(dev)
+    with torch.no_grad():
+        for i in range(warmup):
+            call(sets[i % len(sets)])
+        torch.cuda.synchronize()
+        sampler = ClockSampler(dev.index or 0)
+        sampler.start()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for i in range(args.steps):
+            call(sets[i % len(sets)])
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        clocks = sampler.stop()
+        ms = ev0.elapsed_time(ev1)
+        spans = float(sum(sets[i % len(sets)]["span_offsets"][-1] for i in range(args.steps)))
+        # the kernel alone, on the same batches' factors
+        fac = [span_factors(marker, b["words"], b["classes"]) for b in sets]
+        kcalls = [lambda b=b, f=f: torch.ops.vf_b200.span_scores(f[0], f[1], b["span_idx"], f[2], f[3],
+                                                                  *(b[k] for k in offs), torch.float32)
+                  for b, f in zip(sets, fac)]
+        for i in range(warmup):
+            kcalls[i % len(kcalls)]()
+        torch.cuda.synchronize()
+        ek0, ek1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ek0.record(stream)
+        for i in range(args.steps):
+            kcalls[i % len(kcalls)]()
+        ek1.record(stream)
+        torch.cuda.synchronize()
+        kms = ek0.elapsed_time(ek1) / args.steps
+    K4 = 4 * W.SPAN_HIDDEN
+    mma_flops = sum(2.0 * K4 * sum((b["span_offsets"][g + 1] - b["span_offsets"][g]) *
+                                   (b["class_offsets"][g + 1] - b["class_offsets"][g])
+                                   for g in range(len(b["span_offsets"]) - 1)) for b in sets) / len(sets)
+    from vf_b200 import dist as VD
+    ms_max, spans_all, _ = VD.reduce_timing(ms, spans, 0.0, dev)
+    value = spans_all / (ms_max * 1e-3)
+    e2e = None
+    if not args.no_e2e:
+        b0 = sets[0]
+        host = {"words": b0["words"].cpu().pin_memory(), "span_idx": b0["span_idx"].cpu().pin_memory(),
+                "classes": b0["classes"].cpu().pin_memory(), **{k: b0[k] for k in offs}}
+        n_e2e = max(3, min(args.steps, 10))
+        with torch.no_grad():
+            ems, h2d, d2h = pipelined_e2e(dev, host, call, n_e2e, world)
+        e2e = {"value": b0["span_offsets"][-1] * world * n_e2e / (ems * 1e-3), "unit": "spans/s", "pipelined": True,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": n_e2e}
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    achieved = mma_flops / (kms * 1e-3) / 1e12
+    return {"metric": METRIC, "value": value, "unit": "spans/s", "n_gpus": world, "steps": args.steps,
+            "warmup": warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": GLINER_SPAN_CONFIG,
+            "l2": "4 rotating request batches (~30 MB inputs each) and 92 MB of weights; no flush",
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"], "unit": "TFLOP/s",
+                         "frac": achieved / peaks["bf16"], "traffic": committed_traffic(args.workload),
+                         "peak_source": f"{peaks['source']} bf16 dense (burst)",
+                         "what": "span-score kernel alone: 2 x spans x 4D x classes per launch",
+                         "kernel_ms": kms, "algorithmic_flops_per_launch": mma_flops},
+            "gpu_launches": 2 * args.steps, "clocks": clocks, "e2e": e2e,
+            **({"cpu_baseline": gliner_span_cpu_baseline()} if world == 1 and not args.no_cpu_baseline else {})}
+
+
 # ----------------------------------------------------------------------------- attention lines
 def reference_triton_kernels():
     """The reference's own Triton modules (kernels/flash_attention_rpb.py,
@@ -764,6 +886,8 @@ def reference_line(args, name: str) -> dict:
         cb, cfg = gated_act_cpu_baseline(), {"workload": name}
     elif name == "deberta_add_ln":
         cb, cfg = add_layer_norm_cpu_baseline(), {"workload": name}
+    elif name == "gliner_span":
+        cb, cfg = gliner_span_cpu_baseline(), GLINER_SPAN_CONFIG
     else:
         cb = cpu_baseline(name, None, budget_s=max(5.0, min(60.0, 2.0 * args.steps)))
         cfg = attention_config(name)
@@ -845,6 +969,8 @@ def main():
         line = run_gated_act(args, world, rank, dev, warmup)
     elif headline == "deberta_add_ln":
         line = run_add_layer_norm(args, world, rank, dev, warmup)
+    elif headline == "gliner_span":
+        line = run_gliner_span(args, world, rank, dev, warmup)
     else:
         line = run_attention(args, headline, args.steps, world, rank, dev, warmup, cpu_base)
     if subs:

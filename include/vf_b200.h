@@ -262,6 +262,55 @@ typedef struct {
 int vf_add_layer_norm_fwd(const vf_add_layer_norm_args_t* args, void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * GLiNER span scores.  Replaces the span-representation MLP and the class einsum of
+ * poolers/gliner.py:118-140 (SpanMarkerV0.forward) and :285-289 (GLiNERSpanPooler.forward:
+ * `span_rep = self.span_rep(we, span_idx_masked)`, `scores = torch.einsum("BLKD,BCD->BLKC",
+ * span_rep, pe)`); the same marker scores GLiNER2 fields (poolers/gliner2.py:230-259, :384-404).
+ * With out_project = Linear(2D, 4D) [W1 = (W1a | W1b), b1] -> ReLU -> Linear(4D, D) [W2, b2],
+ * the caller passes per-word and per-class products instead of the per-span MLP:
+ *   start_proj = relu(start_rep) W1a^T + b1     [words, K]   (K = 4D)
+ *   end_proj   = relu(end_rep)   W1b^T          [words, K]
+ *   classes    = pe W2                          [classes, K]
+ *   class_bias = pe . b2 (fp32)                 [classes], or NULL
+ * and the kernel computes, for span s = (i_s, j_s) of segment g and class c of segment g,
+ *   out[s, c] = class_bias[c] + sum_k relu(start_proj[i_s, k] + end_proj[j_s, k]) * classes[c, k]
+ * (relu(a + b) rounded once to the 16-bit dtype; products and sum in fp32 on the tensor cores),
+ * which equals einsum(out_project(relu(cat(start_rep[i], end_rep[j]))), pe) of the reference.
+ * Span indices are local to the segment and clamped to [0, words_g - 1] as the reference's
+ * extract_elements clamps them (a masked span, index (0, 0), scores word 0's span).
+ * Segments (sentences) g = 0 .. num_segments - 1 are independent: words [word_offsets[g],
+ * word_offsets[g+1]) of start_proj / end_proj, spans [span_offsets[g], span_offsets[g+1]) of
+ * span_idx, classes [class_offsets[g], class_offsets[g+1]) of classes / class_bias; the
+ * offsets are HOST arrays of num_segments + 1 non-decreasing entries.  Segment g's scores are a
+ * [spans_g, classes_g] row-major block of `out`, the blocks back to back in segment order
+ * (out holds sum_g spans_g * classes_g elements of out_dtype).
+ * start_proj, end_proj, classes: 16-bit (f16 / bf16) rows with unit column stride, 16-byte
+ * aligned rows, row strides >= K in elements; K a multiple of 64.  span_idx: int64 when
+ * span_idx_int64 != 0, else int32; element (s, e) at s * idx_stride_span + e * idx_stride_pair.
+ * ------------------------------------------------------------------------------------ */
+typedef struct {
+  vf_dtype_t dtype;
+  const void* start_proj;
+  const void* end_proj;
+  int64_t start_row_stride, end_row_stride;
+  int64_t K;
+  const void* span_idx;
+  int32_t span_idx_int64;
+  int64_t idx_stride_span, idx_stride_pair;
+  const void* classes;
+  int64_t class_row_stride;
+  const float* class_bias;
+  void* out;
+  vf_dtype_t out_dtype;
+  int32_t num_segments;
+  const int64_t* word_offsets;
+  const int64_t* span_offsets;
+  const int64_t* class_offsets;
+} vf_span_scores_args_t;
+
+int vf_span_scores_fwd(const vf_span_scores_args_t* args, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Host-side bucket functions (no GPU needed).  These are the exact integer outputs the
  * kernels use; they restate, in float32 arithmetic like the reference's torch code:
  *  - models/mt5/mt5_encoder.py:125 T5RelativePositionBias._relative_position_bucket

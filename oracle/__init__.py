@@ -19,6 +19,7 @@ It restates, in plain PyTorch on the CPU, the reference's own algorithms for the
   * DeBERTa layer:    models/deberta_v2/deberta_v2_encoder.py:332-487 (_pytorch_forward)
   * DeBERTa fused:    the caller's products q @ Kr^T, k @ Qr^T (:275-286) + the op above
   * mT5 FFN act:      kernels/ff_fused.py:23-74 (fused_gelu_mul_dropout's kernel, no dropout)
+  * GLiNER spans:     poolers/gliner.py:26-45, :118-140, :285-289 (SpanMarkerV0 + class einsum)
 
 Parity pinning: tests/golden/make_golden.py runs the reference's own functions (imported
 from the read-only reference checkout in the build container) and commits their outputs
@@ -38,3 +39,10 @@ from .rpb import (  # noqa: F401
 )
 from .ffn import gated_act_ref  # noqa: F401,E402
 from .layernorm import add_layer_norm_ref  # noqa: F401,E402
+from .span import (  # noqa: F401,E402
+    span_factors_ref,
+    span_rep_ref,
+    span_scores_factored_ref,
+    span_scores_from_factors_ref,
+    span_scores_ref,
+)

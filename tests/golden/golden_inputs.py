@@ -79,3 +79,29 @@ def deberta_layer_case(name: str = "deberta_layer"):
     mask = (torch.arange(L)[None, :] < torch.tensor(lens)[:, None]).to(torch.int64)
     return dict(hidden=hidden, mask=mask, rel=rel, num_heads=H, position_buckets=pb,
                 max_relative_positions=mr, lens=torch.tensor(lens, dtype=torch.int32), **w, **b)
+
+
+def span_case(name: str = "gliner_span"):
+    """Inputs for the GLiNER span marker + class einsum (poolers/gliner.py:118-140, :285-289):
+    word states h [1, L, D], the reference's default span enumeration (start i, width w,
+    end i + w; spans ending past the sentence masked to (0, 0)), the marker's weights as
+    {name: tensor} with nn.Linear's [out, in] layout, and class embeddings pe [1, C, D]."""
+    if name == "gliner_span":
+        L, D, W, C, true_len, seed = 37, 64, 5, 7, 33, 31
+    else:
+        raise KeyError(name)
+    g = torch.Generator().manual_seed(seed)
+    h = _bf16(torch.randn(1, L, D, generator=g))
+    w = {}
+    for pre, din, dout in (("start", D, D), ("end", D, D), ("out", 2 * D, D)):
+        w[f"{pre}_w1"] = _bf16(torch.randn(4 * dout, din, generator=g) * 0.05)
+        w[f"{pre}_b1"] = _bf16(torch.randn(4 * dout, generator=g) * 0.05)
+        w[f"{pre}_w2"] = _bf16(torch.randn(dout, 4 * dout, generator=g) * 0.05)
+        w[f"{pre}_b2"] = _bf16(torch.randn(dout, generator=g) * 0.05)
+    pe = _bf16(torch.randn(1, C, D, generator=g))
+    starts = torch.arange(L).repeat_interleave(W)
+    widths = torch.arange(W).repeat(L)
+    idx = torch.stack([starts, starts + widths], dim=-1)
+    mask = (idx[:, 0] < true_len) & (idx[:, 1] < true_len)
+    span_idx = (idx * mask.unsqueeze(-1)).unsqueeze(0)
+    return dict(h=h, weights=w, pe=pe, span_idx=span_idx, max_width=W)

@@ -16,7 +16,9 @@ What it records (all from reference functions, never from this repository's code
     _make_contiguous_additive_bias (:75) + SDPA with scale 1.0, the fallback math of
     T5SelfAttention.forward (:285-316);
   * DeBERTa-v2 layer context: DisentangledSelfAttentionV2._pytorch_forward (:332) built on
-    vLLM's CPU linears with the case's weights.
+    vLLM's CPU linears with the case's weights;
+  * GLiNER span scores: poolers/gliner.py SpanMarkerV0.forward (:133-140) with the case's
+    weights, in float64, and the pooler's einsum (:289).
 """
 from __future__ import annotations
 
@@ -130,6 +132,25 @@ def main():
     for key in ("hidden", "wq", "wk", "wv", "rel"):
         out[f"deberta_layer_sha_{key}"] = np.array(gi.sha(c[key]))
     del ctx
+
+    # ---------------- GLiNER span marker + class einsum, float64
+    from poolers.gliner import SpanMarkerV0
+    c = gi.span_case()
+    D = c["h"].shape[-1]
+    marker = SpanMarkerV0(D, c["max_width"], dropout=0.0).double().eval()
+    with torch.no_grad():
+        for pre, seq in (("start", marker.project_start), ("end", marker.project_end), ("out", marker.out_project)):
+            seq[0].weight.copy_(c["weights"][f"{pre}_w1"])
+            seq[0].bias.copy_(c["weights"][f"{pre}_b1"])
+            seq[3].weight.copy_(c["weights"][f"{pre}_w2"])
+            seq[3].bias.copy_(c["weights"][f"{pre}_b2"])
+        rep = marker(c["h"].double(), c["span_idx"])
+        scores = torch.einsum("BLKD,BCD->BLKC", rep, c["pe"].double()).squeeze(0)
+    out["gliner_span_out"] = scores.numpy()
+    for key in ("h", "pe", "span_idx"):
+        out[f"gliner_span_sha_{key}"] = np.array(gi.sha(c[key]))
+    for key, t in sorted(c["weights"].items()):
+        out[f"gliner_span_sha_{key}"] = np.array(gi.sha(t))
 
     np.savez_compressed(args.out, **out)
     print(f"wrote {args.out}: {sorted(out)}")

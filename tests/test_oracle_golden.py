@@ -79,3 +79,17 @@ def test_deberta_position_index_symmetry():
     rel = torch.arange(300)[:, None] - torch.arange(300)[None, :]
     hf = torch.clamp(-oracle.deberta_log_bucket_ref(-rel, 64, 128) + 64, 0, 127)
     assert torch.equal(idx, hf)
+
+
+def test_gliner_span_oracle_matches_reference():
+    c = gi.span_case()
+    for key in ("h", "pe", "span_idx"):
+        assert gi.sha(c[key]) == str(G[f"gliner_span_sha_{key}"])
+    for key, t in c["weights"].items():
+        assert gi.sha(t) == str(G[f"gliner_span_sha_{key}"])
+    ref = torch.from_numpy(G["gliner_span_out"])
+    out = oracle.span_scores_ref(c["h"], c["span_idx"], c["weights"], c["pe"], c["max_width"])
+    assert (out - ref).abs().max().item() < 1e-12
+    # The factored form the GPU kernel evaluates equals the reference's order of operations.
+    fac = oracle.span_scores_factored_ref(c["h"], c["span_idx"], c["weights"], c["pe"], c["max_width"])
+    assert (fac - ref).abs().max().item() < 1e-12

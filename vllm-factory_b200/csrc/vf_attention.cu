@@ -1469,7 +1469,10 @@ int vf_device_error(int32_t clear) {
   unsigned int fused_word = 0;
   e = vf::fused_take_error_word(clear != 0, &fused_word);
   if (e != cudaSuccess) return fail(VF_ECUDA, std::string("reading the device error word: ") + cudaGetErrorString(e));
-  return static_cast<int>((word | fused_word) & 0x7fffffff);
+  unsigned int span_word = 0;
+  e = vf::span_take_error_word(clear != 0, &span_word);
+  if (e != cudaSuccess) return fail(VF_ECUDA, std::string("reading the device error word: ") + cudaGetErrorString(e));
+  return static_cast<int>((word | fused_word | span_word) & 0x7fffffff);
 }
 
 int vf_selftest_wait_timeout(int64_t limit_cycles, void* stream) {

@@ -36,4 +36,7 @@ PFN_cuTensorMapEncodeTiled_v12000 host_encode_fn();
 // cleared in one atomic operation.
 cudaError_t fused_take_error_word(bool clear, unsigned int* word);
 
+// The same for the span-score kernel file (vf_span.cu).
+cudaError_t span_take_error_word(bool clear, unsigned int* word);
+
 }  // namespace vf

@@ -540,6 +540,100 @@ at::Tensor add_layer_norm_cpu(const at::Tensor&, const at::Tensor&, const at::Te
   TORCH_CHECK(false, "vf_b200: x and residual must be CUDA tensors (no CPU implementation)");
 }
 
+// ---------------------------------------------------------------- GLiNER span scores
+// Rows of a 2-D 16-bit operand as the kernel reads them: unit column stride, 16-byte aligned
+// base and row stride (else a contiguous copy).
+at::Tensor span_rows(const at::Tensor& t) {
+  const int64_t es = t.element_size();
+  const bool ok = t.stride(1) == 1 && (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0 &&
+                  (t.size(0) <= 1 || ((t.stride(0) * es) % 16 == 0 && t.stride(0) >= t.size(1)));
+  return ok ? t : t.contiguous();
+}
+
+int64_t span_scores_numel(at::IntArrayRef span_offsets, at::IntArrayRef class_offsets) {
+  TORCH_CHECK(span_offsets.size() == class_offsets.size() && !span_offsets.empty(),
+              "vf_b200: span_offsets and class_offsets must both have num_segments + 1 entries");
+  int64_t n = 0;
+  for (size_t g = 0; g + 1 < span_offsets.size(); ++g) {
+    const int64_t S = span_offsets[g + 1] - span_offsets[g], C = class_offsets[g + 1] - class_offsets[g];
+    TORCH_CHECK(S >= 0 && C >= 0, "vf_b200: span / class offsets must not decrease");
+    n += S * C;
+  }
+  return n;
+}
+
+// Scores of every (span, class) pair of every segment, [sum_g spans_g * classes_g] in
+// out_dtype, segment g's [spans_g, classes_g] block after the previous segments' blocks.
+at::Tensor span_scores(const at::Tensor& start_in, const at::Tensor& end_in, const at::Tensor& idx_in,
+                       const at::Tensor& classes_in, const std::optional<at::Tensor>& bias_opt,
+                       at::IntArrayRef word_offsets, at::IntArrayRef span_offsets, at::IntArrayRef class_offsets,
+                       at::ScalarType out_dtype) {
+  require_cuda(start_in, "start_proj");
+  require_cuda(end_in, "end_proj");
+  require_cuda(idx_in, "span_idx");
+  require_cuda(classes_in, "classes");
+  TORCH_CHECK(start_in.dim() == 2 && end_in.dim() == 2 && classes_in.dim() == 2,
+              "vf_b200: start_proj, end_proj and classes must be 2-D [rows, K]");
+  TORCH_CHECK(start_in.sizes() == end_in.sizes(), "vf_b200: start_proj and end_proj must have the same shape");
+  TORCH_CHECK(classes_in.size(1) == start_in.size(1), "vf_b200: classes must have K = ", start_in.size(1), " columns");
+  TORCH_CHECK(start_in.scalar_type() == end_in.scalar_type() && start_in.scalar_type() == classes_in.scalar_type(),
+              "vf_b200: start_proj, end_proj and classes must share a dtype");
+  TORCH_CHECK(idx_in.dim() == 2 && idx_in.size(1) == 2, "vf_b200: span_idx must be [spans, 2]");
+  TORCH_CHECK(idx_in.scalar_type() == at::kLong || idx_in.scalar_type() == at::kInt,
+              "vf_b200: span_idx must be int64 or int32");
+  TORCH_CHECK(word_offsets.size() == span_offsets.size(), "vf_b200: word_offsets must have num_segments + 1 entries");
+  TORCH_CHECK(out_dtype == at::kFloat || out_dtype == at::kHalf || out_dtype == at::kBFloat16,
+              "vf_b200: out_dtype must be float32, float16 or bfloat16");
+  const int64_t G = static_cast<int64_t>(span_offsets.size()) - 1;
+  TORCH_CHECK(G <= INT32_MAX, "vf_b200: too many segments");
+  TORCH_CHECK(word_offsets.back() <= start_in.size(0), "vf_b200: word_offsets run past start_proj's rows");
+  TORCH_CHECK(span_offsets.back() <= idx_in.size(0), "vf_b200: span_offsets run past span_idx's rows");
+  TORCH_CHECK(class_offsets.back() <= classes_in.size(0), "vf_b200: class_offsets run past classes' rows");
+  c10::cuda::CUDAGuard guard(start_in.device());
+  at::Tensor out = at::empty({span_scores_numel(span_offsets, class_offsets)}, start_in.options().dtype(out_dtype));
+  if (out.numel() == 0) return out;
+  const at::Tensor u = span_rows(start_in), v = span_rows(end_in), c = span_rows(classes_in);
+  at::Tensor bias;
+  if (bias_opt.has_value() && bias_opt->defined()) {
+    require_cuda(*bias_opt, "class_bias");
+    TORCH_CHECK(bias_opt->dim() == 1 && bias_opt->size(0) >= class_offsets.back(),
+                "vf_b200: class_bias must be 1-D with a value per class");
+    bias = bias_opt->to(at::kFloat).contiguous();
+  }
+  vf_span_scores_args_t a{};
+  a.dtype = dtype_code(u);
+  a.start_proj = u.data_ptr();
+  a.end_proj = v.data_ptr();
+  a.start_row_stride = u.size(0) > 1 ? u.stride(0) : u.size(1);
+  a.end_row_stride = v.size(0) > 1 ? v.stride(0) : v.size(1);
+  a.K = u.size(1);
+  a.span_idx = idx_in.data_ptr();
+  a.span_idx_int64 = idx_in.scalar_type() == at::kLong ? 1 : 0;
+  a.idx_stride_span = idx_in.stride(0);
+  a.idx_stride_pair = idx_in.stride(1);
+  a.classes = c.data_ptr();
+  a.class_row_stride = c.size(0) > 1 ? c.stride(0) : c.size(1);
+  a.class_bias = bias.defined() ? bias.data_ptr<float>() : nullptr;
+  a.out = out.data_ptr();
+  a.out_dtype = dtype_code(out);
+  a.num_segments = static_cast<int32_t>(G);
+  a.word_offsets = word_offsets.data();
+  a.span_offsets = span_offsets.data();
+  a.class_offsets = class_offsets.data();
+  check_rc(vf_span_scores_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
+  return out;
+}
+at::Tensor span_scores_meta(const at::Tensor& start_proj, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                            const std::optional<at::Tensor>&, at::IntArrayRef, at::IntArrayRef span_offsets,
+                            at::IntArrayRef class_offsets, at::ScalarType out_dtype) {
+  return at::empty({span_scores_numel(span_offsets, class_offsets)}, start_proj.options().dtype(out_dtype));
+}
+at::Tensor span_scores_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                           const std::optional<at::Tensor>&, at::IntArrayRef, at::IntArrayRef, at::IntArrayRef,
+                           at::ScalarType) {
+  TORCH_CHECK(false, "vf_b200: start_proj must be a CUDA tensor (no CPU implementation)");
+}
+
 // Shape functions for tracing (torch.compile / fake tensors).
 at::Tensor rpb_attention_meta(const at::Tensor& q, const at::Tensor&, const at::Tensor&,
                               const std::optional<at::Tensor>&, int64_t, int64_t, bool,
@@ -606,6 +700,8 @@ TORCH_LIBRARY(vf_b200, m) {
   m.def("deberta_attention_fused_varlen(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, int max_seqlen, "
         "Tensor? rel_key, Tensor? rel_query, bool causal, float? sm_scale, int position_buckets, "
         "int max_relative_distance, bool use_log_bucket) -> Tensor");
+  m.def("span_scores(Tensor start_proj, Tensor end_proj, Tensor span_idx, Tensor classes, Tensor? class_bias, "
+        "int[] word_offsets, int[] span_offsets, int[] class_offsets, ScalarType out_dtype) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, CUDA, m) {
@@ -617,6 +713,7 @@ TORCH_LIBRARY_IMPL(vf_b200, CUDA, m) {
   m.impl("deberta_attention_fused_varlen", &deberta_attention_fused_varlen);
   m.impl("gated_act", &gated_act);
   m.impl("add_layer_norm", &add_layer_norm);
+  m.impl("span_scores", &span_scores);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
@@ -628,6 +725,7 @@ TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
   m.impl("deberta_attention_fused_varlen", &deberta_attention_fused_varlen_cpu);
   m.impl("gated_act", &gated_act_cpu);
   m.impl("add_layer_norm", &add_layer_norm_cpu);
+  m.impl("span_scores", &span_scores_cpu);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
@@ -639,4 +737,5 @@ TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
   m.impl("deberta_attention_fused_varlen", &deberta_attention_varlen_meta);
   m.impl("gated_act", &gated_act_meta);
   m.impl("add_layer_norm", &add_layer_norm_meta);
+  m.impl("span_scores", &span_scores_meta);
 }

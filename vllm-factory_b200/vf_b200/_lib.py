@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "vf_deberta_attention_fused_noalloc_fwd",
     "vf_gated_act_fwd",
     "vf_add_layer_norm_fwd",
+    "vf_span_scores_fwd",
     "vf_t5_relative_bucket",
     "vf_deberta_log_bucket",
     "vf_last_error",
@@ -109,6 +110,30 @@ class AddLayerNormArgs(ctypes.Structure):
         ("residual_row_stride", ctypes.c_int64),
         ("out_row_stride", ctypes.c_int64),
         ("eps", ctypes.c_float),
+    ]
+
+
+class SpanScoresArgs(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_int),
+        ("start_proj", ctypes.c_void_p),
+        ("end_proj", ctypes.c_void_p),
+        ("start_row_stride", ctypes.c_int64),
+        ("end_row_stride", ctypes.c_int64),
+        ("K", ctypes.c_int64),
+        ("span_idx", ctypes.c_void_p),
+        ("span_idx_int64", ctypes.c_int32),
+        ("idx_stride_span", ctypes.c_int64),
+        ("idx_stride_pair", ctypes.c_int64),
+        ("classes", ctypes.c_void_p),
+        ("class_row_stride", ctypes.c_int64),
+        ("class_bias", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("out_dtype", ctypes.c_int),
+        ("num_segments", ctypes.c_int32),
+        ("word_offsets", ctypes.POINTER(ctypes.c_int64)),
+        ("span_offsets", ctypes.POINTER(ctypes.c_int64)),
+        ("class_offsets", ctypes.POINTER(ctypes.c_int64)),
     ]
 
 
@@ -200,6 +225,8 @@ def load() -> ctypes.CDLL:
         lib.vf_gated_act_fwd.restype = ctypes.c_int
         lib.vf_add_layer_norm_fwd.argtypes = [ctypes.POINTER(AddLayerNormArgs), ctypes.c_void_p]
         lib.vf_add_layer_norm_fwd.restype = ctypes.c_int
+        lib.vf_span_scores_fwd.argtypes = [ctypes.POINTER(SpanScoresArgs), ctypes.c_void_p]
+        lib.vf_span_scores_fwd.restype = ctypes.c_int
         lib.vf_t5_relative_bucket.argtypes = [ctypes.c_int32] * 5 + [ctypes.POINTER(ctypes.c_int32)]
         lib.vf_t5_relative_bucket.restype = ctypes.c_int
         lib.vf_deberta_log_bucket.argtypes = [ctypes.c_int32] * 4 + [ctypes.POINTER(ctypes.c_int32)]

@@ -167,3 +167,54 @@ def rank_lengths(kind: str, rank: int):
     else:
         base = torch.randint(64, 512 + 1, (8,), generator=_gen(2000))
     return torch.roll(base, shifts=rank)
+
+
+# ----------------------------------------------------------------------------- GLiNER span head
+SPAN_HIDDEN = 1024        # GLiNER-large (DeBERTa-v3-large backbone) hidden size
+SPAN_MAX_WIDTH = 12
+SPAN_REQUESTS = 64
+
+
+def gliner_span_marker(seed: int = 6000, device="cuda", D: int = SPAN_HIDDEN, dtype=torch.bfloat16):
+    """A SpanMarkerV0-shaped module (poolers/gliner.py:118-140: project_start / project_end
+    Linear(D, 4D) -> ReLU -> Dropout -> Linear(4D, D), out_project Linear(2D, 4D) -> ReLU ->
+    Dropout -> Linear(4D, D)) with weights and biases ~ N(0, 0.02), eval mode."""
+    from torch import nn
+
+    def proj(din, dout):
+        return nn.Sequential(nn.Linear(din, 4 * dout), nn.ReLU(), nn.Dropout(0.0), nn.Linear(4 * dout, dout))
+
+    m = nn.Module()
+    m.project_start, m.project_end, m.out_project = proj(D, D), proj(D, D), proj(2 * D, D)
+    g = _gen(seed)
+    with torch.no_grad():
+        for p in m.parameters():
+            p.copy_(torch.randn(p.shape, generator=g) * 0.02)
+    return m.to(device=device, dtype=dtype).eval()
+
+
+def gliner_span_batch(seed: int = 6100, device="cuda", n_req: int = SPAN_REQUESTS, D: int = SPAN_HIDDEN,
+                      W: int = SPAN_MAX_WIDTH, dtype=torch.bfloat16):
+    """One vLLM batch for the span head: n_req requests with word counts ~ U[32, 384] and
+    entity-label counts ~ U[3, 25]; word / class states ~ N(0, 1); every (start, width) span
+    with widths < W, spans ending past the text masked to (0, 0) as the pooler masks them.
+    Returns packed words [sum W_g, D], span_idx [sum W_g * W, 2] int64, classes [sum C_g, D]
+    and the three offset lists."""
+    g = _gen(seed)
+    n_words = torch.randint(32, 385, (n_req,), generator=g).tolist()
+    n_cls = torch.randint(3, 26, (n_req,), generator=g).tolist()
+    words = torch.randn(sum(n_words), D, generator=g).to(dtype)
+    classes = torch.randn(sum(n_cls), D, generator=g).to(dtype)
+    idx = []
+    for n in n_words:
+        first = torch.arange(n).repeat_interleave(W)
+        last = first + torch.arange(W).repeat(n)
+        idx.append(torch.stack([first, last], -1) * (last < n).unsqueeze(-1))
+    span_idx = torch.cat(idx, 0)
+    wo, so, co = [0], [0], [0]
+    for n, c in zip(n_words, n_cls):
+        wo.append(wo[-1] + n)
+        so.append(so[-1] + n * W)
+        co.append(co[-1] + c)
+    return dict(words=words.to(device), span_idx=span_idx.to(device), classes=classes.to(device),
+                word_offsets=wo, span_offsets=so, class_offsets=co, n_words=n_words, n_classes=n_cls)
