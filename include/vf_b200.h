@@ -237,6 +237,30 @@ typedef struct {
 int vf_gated_act_fwd(const vf_gated_act_args_t* args, void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * Linear + activation of the DeBERTa feed-forward: out = act(x W^T + bias), the activation
+ * applied to the fp32 accumulator in the GEMM's epilogue.  Replaces
+ * models/deberta_v2/deberta_v2_encoder.py:547-550 (DebertaV2Intermediate.forward:
+ * `self.dense(hidden_states)` then `self.intermediate_act_fn`, ACT2FN["gelu"] = exact GELU),
+ * two torch calls with the [rows, N] intermediate in HBM between them.
+ * x: [rows, K], weight: [N, K] (nn.Linear layout), bias: [N] (required), out: [rows, N];
+ * one 16-bit dtype, unit column strides, row strides in elements; K, N and every row stride
+ * multiples of 8, pointers 16-byte aligned; out must not overlap the inputs.  act:
+ * VF_ACT_GELU_ERF (0.5 x (1 + erf(x / sqrt 2))) is the one built.
+ * ------------------------------------------------------------------------------------ */
+typedef struct {
+  vf_dtype_t dtype;
+  const void* x;
+  const void* weight;
+  const void* bias;
+  void* out;
+  int64_t rows, K, N;
+  int64_t x_row_stride, weight_row_stride, out_row_stride;
+  int32_t act;
+} vf_linear_act_args_t;
+
+int vf_linear_act_fwd(const vf_linear_act_args_t* args, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Residual add + LayerNorm of the DeBERTa-v2 encoder: out = LayerNorm(x + residual) with
  * weight and bias over the last dimension.  Replaces the two torch kernels of
  * models/deberta_v2/deberta_v2_encoder.py:507 and :566 (`self.LayerNorm(hidden_states +

@@ -19,6 +19,7 @@ It restates, in plain PyTorch on the CPU, the reference's own algorithms for the
   * DeBERTa layer:    models/deberta_v2/deberta_v2_encoder.py:332-487 (_pytorch_forward)
   * DeBERTa fused:    the caller's products q @ Kr^T, k @ Qr^T (:275-286) + the op above
   * mT5 FFN act:      kernels/ff_fused.py:23-74 (fused_gelu_mul_dropout's kernel, no dropout)
+  * DeBERTa FFN in:   models/deberta_v2/deberta_v2_encoder.py:547-550 (dense + exact GELU)
   * GLiNER spans:     poolers/gliner.py:26-45, :118-140, :285-289 (SpanMarkerV0 + class einsum)
 
 Parity pinning: tests/golden/make_golden.py runs the reference's own functions (imported
@@ -37,7 +38,7 @@ from .rpb import (  # noqa: F401
     t5_bias_dense_ref,
     t5_relative_bucket_ref,
 )
-from .ffn import gated_act_ref  # noqa: F401,E402
+from .ffn import gated_act_ref, linear_gelu_ref  # noqa: F401,E402
 from .layernorm import add_layer_norm_ref  # noqa: F401,E402
 from .span import (  # noqa: F401,E402
     span_factors_ref,

@@ -25,3 +25,13 @@ def gated_act_ref(gate: torch.Tensor, up, act: int = ACT_GELU_TANH) -> torch.Ten
     else:
         g = g * torch.sigmoid(g)
     return (g if up is None else g * up.float()).to(gate.dtype)
+
+
+def linear_gelu_ref(x: torch.Tensor, weight: torch.Tensor, bias, dtype=torch.float64) -> torch.Tensor:
+    """DebertaV2Intermediate.forward (models/deberta_v2/deberta_v2_encoder.py:547-550): the dense
+    layer (ColumnParallelLinear at one rank: x W^T + b) then ACT2FN["gelu"], the exact GELU
+    0.5 x (1 + erf(x / sqrt 2)); in `dtype` arithmetic."""
+    y = x.to(dtype) @ weight.to(dtype).T
+    if bias is not None:
+        y = y + bias.to(dtype)
+    return 0.5 * y * (1.0 + torch.erf(y * 0.7071067811865476))

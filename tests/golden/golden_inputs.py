@@ -105,3 +105,15 @@ def span_case(name: str = "gliner_span"):
     mask = (idx[:, 0] < true_len) & (idx[:, 1] < true_len)
     span_idx = (idx * mask.unsqueeze(-1)).unsqueeze(0)
     return dict(h=h, weights=w, pe=pe, span_idx=span_idx, max_width=W)
+
+
+def intermediate_case(name: str = "deberta_intermediate"):
+    """Inputs for DebertaV2Intermediate (dense [4E, E] + exact GELU): x [rows, E], weight, bias."""
+    if name != "deberta_intermediate":
+        raise KeyError(name)
+    g = torch.Generator().manual_seed(41)
+    E, rows = 64, 50
+    x = _bf16(torch.randn(rows, E, generator=g))
+    w = _bf16(torch.randn(4 * E, E, generator=g) * 0.1)
+    b = _bf16(torch.randn(4 * E, generator=g) * 0.1)
+    return dict(x=x, weight=w, bias=b)

@@ -17,6 +17,7 @@ What it records (all from reference functions, never from this repository's code
     T5SelfAttention.forward (:285-316);
   * DeBERTa-v2 layer context: DisentangledSelfAttentionV2._pytorch_forward (:332) built on
     vLLM's CPU linears with the case's weights;
+  * DebertaV2Intermediate.forward (:547-550): the dense layer + exact GELU, fp32;
   * GLiNER span scores: poolers/gliner.py SpanMarkerV0.forward (:133-140) with the case's
     weights, in float64, and the pooler's einsum (:289).
 """
@@ -131,6 +132,18 @@ def main():
     out["deberta_layer_out"] = ctx_out.float().numpy()
     for key in ("hidden", "wq", "wk", "wv", "rel"):
         out[f"deberta_layer_sha_{key}"] = np.array(gi.sha(c[key]))
+    # ---------------- DebertaV2Intermediate (dense + ACT2FN["gelu"]), fp32
+    from models.deberta_v2.deberta_v2_encoder import DebertaV2Intermediate
+    c = gi.intermediate_case()
+    E = c["x"].shape[-1]
+    icfg = DebertaV2Config(hidden_size=E, num_attention_heads=1, intermediate_size=4 * E, hidden_act="gelu")
+    inter = DebertaV2Intermediate(icfg, prefix="golden.intermediate").eval()
+    with torch.no_grad():
+        inter.dense.weight.copy_(c["weight"])
+        inter.dense.bias.copy_(c["bias"])
+        out["deberta_intermediate_out"] = inter(c["x"]).float().numpy()
+    for key in ("x", "weight", "bias"):
+        out[f"deberta_intermediate_sha_{key}"] = np.array(gi.sha(c[key]))
     del ctx
 
     # ---------------- GLiNER span marker + class einsum, float64

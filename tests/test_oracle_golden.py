@@ -93,3 +93,12 @@ def test_gliner_span_oracle_matches_reference():
     # The factored form the GPU kernel evaluates equals the reference's order of operations.
     fac = oracle.span_scores_factored_ref(c["h"], c["span_idx"], c["weights"], c["pe"], c["max_width"])
     assert (fac - ref).abs().max().item() < 1e-12
+
+
+def test_deberta_intermediate_oracle_matches_reference():
+    c = gi.intermediate_case()
+    for key in ("x", "weight", "bias"):
+        assert gi.sha(c[key]) == str(G[f"deberta_intermediate_sha_{key}"])
+    out = oracle.linear_gelu_ref(c["x"], c["weight"], c["bias"])
+    ref = torch.from_numpy(G["deberta_intermediate_out"]).double()
+    assert (out - ref).abs().max().item() < 2e-5

@@ -830,10 +830,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             // Tiles whose key mask is all zero read a zero row instead of the mask.
             const float* rb = saturated ? rbias + (r_lo >= R ? 2 * R + kRPad : 0)
                                         : rbias + (k0 - m + R + kRPad);
-            const float2* kb = kadd ? kb2 : reinterpret_cast<const float2*>(zero_row);
+            if (kadd) {
 #pragma unroll
-            for (int j = 0; j < kBN / 2; ++j)
-              x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(make_float2(rb[2 * j], rb[2 * j + 1]), kb[j]));
+              for (int j = 0; j < kBN / 2; ++j)
+                x2[j] = __ffma2_rn(x2[j], sc2, __fadd2_rn(make_float2(rb[2 * j], rb[2 * j + 1]), kb2[j]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, make_float2(rb[2 * j], rb[2 * j + 1]));
+            }
           }
           if (edge) {
 #pragma unroll
