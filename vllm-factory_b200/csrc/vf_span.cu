@@ -11,9 +11,12 @@
 //     score[s, c] = pb[c] + sum_k relu(U[i_s, k] + V[j_s, k]) * P[c, k]
 // The caller forms U, V, P, pb (cuBLAS GEMMs over words and classes, not spans); this file
 // does the per-span part: one CTA per 128 spans builds the A operand relu(U[i] + V[j]) in
-// shared memory, 64 K-columns per stage, and multiplies it by the TMA-staged class rows on
-// the tensor cores.  The reference's [spans, 2D] / [spans, 4D] / [spans, D] intermediates
-// never exist.
+// tensor memory (each span row is its thread's TMEM lane, 64 K-columns per stage, written
+// with tcgen05.st) and multiplies it by the TMA-staged class rows on the tensor cores, A read
+// from TMEM.  The tile's word rows come in by TMA with the class rows when its start and end
+// words each fit 32 consecutive rows (always so for the reference's default enumeration of
+// spans); other tiles load their rows directly.  The reference's [spans, 2D] / [spans, 4D] / [spans, D] intermediates never
+// exist, and A never passes through shared memory.
 //
 // Several sentences (segments) go in one launch: segment g has its own word rows, spans and
 // class rows, and its scores form a [spans_g, classes_g] row-major block of the output.  The
@@ -37,16 +40,24 @@ namespace vf {
 namespace span {
 
 constexpr int kTile = 128;             // spans per CTA: UMMA M, one row-building thread per span
-constexpr int kKStep = 64;             // K elements per stage: one 128-byte swizzled row per span
-constexpr int kStages = 4;
+constexpr int kKStep = 64;             // K elements per stage (32 TMEM columns of bf16 / f16 pairs)
+constexpr int kStages = 3;
+constexpr int kACols = 32;             // TMEM columns of one A stage
+constexpr int kAccCol = kStages * kACols;   // first TMEM column of the fp32 accumulator
 constexpr int kThreads = 192;          // warps 0-3 rows + epilogue, warp 4 TMA, warp 5 UMMA
-constexpr int kATile = kTile * 128;    // 16 KB of A per stage
+#ifndef VF_SPAN_MIN_BLOCKS
+#define VF_SPAN_MIN_BLOCKS 3
+#endif
+constexpr int kMinBlocks = VF_SPAN_MIN_BLOCKS;   // CTAs per SM the register budget allows (latency hiding)
 constexpr int kMaxN = 256;             // classes per CTA (UMMA N)
 constexpr int kMaxSeg = 256;           // segments per launch (kernel-parameter tables)
-constexpr int kSmemMax = 1024 + kStages * (kATile + kMaxN * 128) + 256;
+constexpr int kRowBox = 32;            // word rows of one staged U / V box
+constexpr int kBoxBytes = kRowBox * 128;    // 4 KB: 32 rows x 64 columns of 16-bit
+constexpr int kSmemMax = 1024 + kStages * (kMaxN * 128 + 2 * kBoxBytes) + 256;
 
 struct __align__(64) Params {
   CUtensorMap tm_cls;                  // classes [C_total, K], box 64 x npad, 128-byte swizzle
+  CUtensorMap tm_u, tm_v;              // start_proj / end_proj [W_total, K], box 64 x kRowBox, 128-byte swizzle
   const void* u;
   const void* v;
   long long us, vs;                    // row strides of U / V (elements)
@@ -86,18 +97,20 @@ __device__ __forceinline__ void store_out(void* out, long long off, float x, int
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads) span_scores_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, kMinBlocks) span_scores_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int npad = p.npad;
-  uint8_t* sA = smem;                                   // [kStages][128 rows x 128 B], 128-byte swizzle
-  uint8_t* sB = smem + kStages * kATile;                // [kStages][npad rows x 128 B], written by TMA
-  uint64_t* full_a = reinterpret_cast<uint64_t*>(sB + kStages * npad * 128);
-  uint64_t* full_b = full_a + kStages;
+  uint8_t* sB = smem;                                   // [kStages][npad rows x 128 B], written by TMA
+  uint8_t* sU = sB + kStages * npad * 128;              // [kStages][kRowBox rows x 128 B] (staged tiles)
+  uint8_t* sV = sU + kStages * kBoxBytes;
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(sV + kStages * kBoxBytes);
+  uint64_t* full_b = full_a + kStages;                  // class rows (and staged word rows) landed
   uint64_t* empty = full_b + kStages;
   uint64_t* done = empty + kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* rng = reinterpret_cast<int*>(tmem_slot + 2);     // i_min, i_max, j_min, j_max
 
   // This CTA's segment: the last g with tile_off[g] <= tile (segments without tiles have
   // tile_off[g] == tile_off[g + 1] and are passed over).
@@ -123,63 +136,95 @@ __global__ void __launch_bounds__(kThreads) span_scores_kernel(const __grid_cons
     }
     mbar_init(done, 1);
     *abort_flag = 0;
+    rng[0] = rng[2] = 0x7fffffff;
+    rng[1] = rng[3] = -1;
     fence_mbar_init();
   }
   if (warp == 5) {
     tmem_alloc(tmem_slot, static_cast<uint32_t>(p.tmem_cols));
     tmem_relinquish();
   }
+  // The tile's span rows (threads 0-127): word indices clamped to the sentence's words, as
+  // the reference's extract_elements clamps them.
+  const int t = threadIdx.x;                                // span row of the tile == TMEM lane
+  int i = 0, j = 0;
+  if (warp < 4) {
+    const int sl = min(s_begin + t, S_g - 1);               // rows past the segment repeat its last span
+    const long long srow = p.span_off[g] + sl;
+    long long i64, j64;
+    if (p.idx64) {
+      const long long* ix = reinterpret_cast<const long long*>(p.idx) + srow * p.idx_ss;
+      i64 = __ldg(ix);
+      j64 = __ldg(ix + p.idx_sp);
+    } else {
+      const int* ix = reinterpret_cast<const int*>(p.idx) + srow * p.idx_ss;
+      i64 = __ldg(ix);
+      j64 = __ldg(ix + p.idx_sp);
+    }
+    const long long last = p.word_len[g] - 1;
+    i = static_cast<int>(min(max(i64, 0LL), last));
+    j = static_cast<int>(min(max(j64, 0LL), last));
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (warp < 4) {
+    atomicMin(&rng[0], i);
+    atomicMax(&rng[1], i);
+    atomicMin(&rng[2], j);
+    atomicMax(&rng[3], j);
+  }
+  __syncthreads();
+  // Staged tile: its start words and its end words each lie within kRowBox consecutive rows (the
+  // reference's default enumeration gives <= ceil(128 / max_width) + 1 and that + max_width - 1),
+  // so every stage brings them in as two TMA boxes; otherwise each thread loads its own rows.
+  const int i_min = rng[0], j_min = rng[2];
+  const bool staged = rng[1] - i_min < kRowBox && rng[3] - j_min < kRowBox;
 
   if (warp < 4) {
     // ---------------------------------------------------------------- A rows + epilogue
-    const int t = threadIdx.x;                                // span row of the tile == TMEM lane
-    const int sl = min(s_begin + t, S_g - 1);                 // rows past the segment repeat its last span
-    const long long srow = p.span_off[g] + sl;
-    long long i, j;
-    if (p.idx64) {
-      const long long* ix = reinterpret_cast<const long long*>(p.idx) + srow * p.idx_ss;
-      i = __ldg(ix);
-      j = __ldg(ix + p.idx_sp);
-    } else {
-      const int* ix = reinterpret_cast<const int*>(p.idx) + srow * p.idx_ss;
-      i = __ldg(ix);
-      j = __ldg(ix + p.idx_sp);
-    }
-    // The reference gathers with indices clamped to the sentence's words (extract_elements).
-    const long long last = p.word_len[g] - 1;
-    i = min(max(i, 0LL), last);
-    j = min(max(j, 0LL), last);
-    const uint4* ur = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.u) + (p.word_off[g] + i) * p.us);
-    const uint4* vr = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.v) + (p.word_off[g] + j) * p.vs);
-    const uint32_t sw = static_cast<uint32_t>(t & 7);
+    const uint4* ur = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.u) + (p.word_off[g] + (long long)i) * p.us);
+    const uint4* vr = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.v) + (p.word_off[g] + (long long)j) * p.vs);
+    const uint32_t ru = static_cast<uint32_t>(i - i_min), rv = static_cast<uint32_t>(j - j_min);   // rows in the boxes
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;   // this warp's TMEM lanes
     bool ok = true;
     for (int kc = 0; kc < nk; ++kc) {
       const int st = kc % kStages;
       uint4 a[8], b[8];
+      if (staged) {
+        ok = mbar_wait(&full_b[st], (kc / kStages) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        const uint8_t* urow = sU + st * kBoxBytes + ru * 128;
+        const uint8_t* vrow = sV + st * kBoxBytes + rv * 128;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        a[q] = __ldg(ur + kc * 8 + q);
-        b[q] = __ldg(vr + kc * 8 + q);
+        for (int q = 0; q < 8; ++q) {   // 16-byte chunk q of a row sits at q ^ (row & 7) (128-byte swizzle)
+          a[q] = *reinterpret_cast<const uint4*>(urow + ((static_cast<uint32_t>(q) ^ (ru & 7u)) << 4));
+          b[q] = *reinterpret_cast<const uint4*>(vrow + ((static_cast<uint32_t>(q) ^ (rv & 7u)) << 4));
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          a[q] = __ldg(ur + kc * 8 + q);
+          b[q] = __ldg(vr + kc * 8 + q);
+        }
       }
       if (kc >= kStages) {
         ok = mbar_wait(&empty[st], ((kc / kStages) - 1) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
       }
-      uint8_t* row = sA + st * kATile + t * 128;
+      // Row t of the A stage: 64 elements as 32 packed pairs, K in column order.
+      uint32_t r[32];
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        uint4 r;
-        r.x = add_relu2<T>(a[q].x, b[q].x);
-        r.y = add_relu2<T>(a[q].y, b[q].y);
-        r.z = add_relu2<T>(a[q].z, b[q].z);
-        r.w = add_relu2<T>(a[q].w, b[q].w);
-        *reinterpret_cast<uint4*>(row + ((static_cast<uint32_t>(q) ^ sw) << 4)) = r;   // 16-byte chunk q of row t
+        r[4 * q + 0] = add_relu2<T>(a[q].x, b[q].x);
+        r[4 * q + 1] = add_relu2<T>(a[q].y, b[q].y);
+        r[4 * q + 2] = add_relu2<T>(a[q].z, b[q].z);
+        r[4 * q + 3] = add_relu2<T>(a[q].w, b[q].w);
       }
-      fence_proxy_async_smem();
+      tmem_st_x32(tmem + lane_base + static_cast<uint32_t>(st * kACols), r);   // waits for the store
+      tc_fence_before();
       mbar_arrive(&full_a[st]);
     }
     // Epilogue: the 128 x npad fp32 accumulator, 16 columns at a time; each thread writes
@@ -193,7 +238,7 @@ __global__ void __launch_bounds__(kThreads) span_scores_kernel(const __grid_cons
       const float* cb = p.cbias != nullptr ? p.cbias + p.class_off[g] + c0 : nullptr;
       for (int cc = 0; cc < npad; cc += 16) {
         uint32_t r[16];
-        tmem_ld_x16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + cc, r);   // collective: every lane
+        tmem_ld_x16(tmem + lane_base + static_cast<uint32_t>(kAccCol + cc), r);   // collective: every lane
         if (mine) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
@@ -208,11 +253,16 @@ __global__ void __launch_bounds__(kThreads) span_scores_kernel(const __grid_cons
     if (lane == 0) {
       int issued = 0;
       const int crow = p.class_off[g] + c0;
+      const int urow0 = p.word_off[g] + i_min, vrow0 = p.word_off[g] + j_min;
       for (int kc = 0; kc < nk; ++kc) {
         const int st = kc % kStages;
         if (kc >= kStages && !mbar_wait(&empty[st], ((kc / kStages) - 1) & 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&full_b[st], static_cast<uint32_t>(npad * 128));
+        mbar_arrive_expect_tx(&full_b[st], static_cast<uint32_t>(npad * 128 + (staged ? 2 * kBoxBytes : 0)));
         tma_load_2d(sB + st * npad * 128, &p.tm_cls, &full_b[st], kc * kKStep, crow);
+        if (staged) {
+          tma_load_2d(sU + st * kBoxBytes, &p.tm_u, &full_b[st], kc * kKStep, urow0);
+          tma_load_2d(sV + st * kBoxBytes, &p.tm_v, &full_b[st], kc * kKStep, vrow0);
+        }
         ++issued;
       }
       // No TMA write may land after the CTA exits: wait for the last fills (time-bounded).
@@ -223,7 +273,7 @@ __global__ void __launch_bounds__(kThreads) span_scores_kernel(const __grid_cons
     // ---------------------------------------------------------------- UMMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(AbFmt<T>::value, kTile, static_cast<uint32_t>(npad), 0, 0);
-      const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+      const uint32_t b0 = smem_u32(sB);
       for (int kc = 0; kc < nk; ++kc) {
         const int st = kc % kStages;
         const uint32_t par = (kc / kStages) & 1;
@@ -231,9 +281,10 @@ __global__ void __launch_bounds__(kThreads) span_scores_kernel(const __grid_cons
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kKStep / 16; ++kk) {
-          const uint64_t ad = smem_desc_sw128(a0 + st * kATile + kk * 32, 16, 1024);
+          // A: 128 lanes x 8 columns (16 K-elements) of the stage in TMEM; B: the class rows.
           const uint64_t bd = smem_desc_sw128(b0 + st * npad * 128 + kk * 32, 16, 1024);
-          umma_ss(tmem, ad, bd, idesc, (kc > 0 || kk > 0) ? 1u : 0u);
+          umma_ts(tmem + kAccCol, tmem + static_cast<uint32_t>(st * kACols + kk * 8), bd, idesc,
+                  (kc > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&empty[st]);
       }
@@ -335,7 +386,7 @@ int vf_span_scores_fwd(const vf_span_scores_args_t* a, void* stream) {
   if (enc == nullptr) return sfail(VF_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
   const int npad = static_cast<int>(std::min<int64_t>(vf::span::kMaxN, (max_c + 15) / 16 * 16));
   int tcols = 32;
-  while (tcols < npad) tcols *= 2;
+  while (tcols < vf::span::kAccCol + npad) tcols *= 2;   // A stages + the accumulator
 
   vf::span::Params prm{};
   {
@@ -349,6 +400,20 @@ int vf_span_scores_fwd(const vf_span_scores_args_t* a, void* stream) {
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return sfail(VF_ECUDA, "classes map: cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    // start_proj / end_proj rows, 32 at a time (a staged tile's start and end words).
+    const void* bases[2] = {a->start_proj, a->end_proj};
+    const int64_t rstr[2] = {a->start_row_stride, a->end_row_stride};
+    CUtensorMap* maps[2] = {&prm.tm_u, &prm.tm_v};
+    for (int w = 0; w < 2; ++w) {
+      cuuint64_t wd[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(std::max<int64_t>(wo[G], 1))};
+      cuuint64_t ws[1] = {static_cast<cuuint64_t>(rstr[w] * 2)};
+      cuuint32_t wb[2] = {static_cast<cuuint32_t>(vf::span::kKStep), static_cast<cuuint32_t>(vf::span::kRowBox)};
+      const CUresult rw = enc(maps[w], ty, 2, const_cast<void*>(bases[w]), wd, ws, wb, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (rw != CUDA_SUCCESS)
+        return sfail(VF_ECUDA, "word-row map: cuTensorMapEncodeTiled failed (" + std::to_string(int(rw)) + ")");
+    }
   }
   prm.u = a->start_proj;
   prm.v = a->end_proj;
@@ -364,7 +429,7 @@ int vf_span_scores_fwd(const vf_span_scores_args_t* a, void* stream) {
   prm.K = static_cast<int>(K);
   prm.npad = npad;
   prm.tmem_cols = tcols;
-  const int smem = 1024 + vf::span::kStages * (vf::span::kATile + npad * 128) + 256;
+  const int smem = 1024 + vf::span::kStages * (npad * 128 + 2 * vf::span::kBoxBytes) + 256;
   const unsigned ych = static_cast<unsigned>((max_c + vf::span::kMaxN - 1) / vf::span::kMaxN);
   if (ych > 65535u) return sfail(VF_EUNSUPPORTED, "more than 65535 x 256 classes in one segment");
   cudaStream_t s = static_cast<cudaStream_t>(stream);

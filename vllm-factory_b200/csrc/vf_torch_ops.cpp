@@ -542,10 +542,10 @@ at::Tensor add_layer_norm_cpu(const at::Tensor&, const at::Tensor&, const at::Te
 }
 
 // ---------------------------------------------------------------- linear + activation
-// act(x W^T + bias) over the last dimension of x (any leading shape), the activation in the
-// GEMM's epilogue (vf_linear_act_fwd).
+// act(x W^T + bias), or act(x W^T) * mul, over the last dimension of x (any leading shape),
+// the activation in the GEMM's epilogue (vf_linear_act_fwd).
 at::Tensor linear_act(const at::Tensor& x_in, const at::Tensor& w_in, const std::optional<at::Tensor>& bias_opt,
-                      int64_t act) {
+                      const std::optional<at::Tensor>& mul_opt, int64_t act) {
   require_cuda(x_in, "x");
   require_cuda(w_in, "weight");
   TORCH_CHECK(w_in.dim() == 2, "vf_b200: weight must be [out_features, in_features]");
@@ -567,8 +567,17 @@ at::Tensor linear_act(const at::Tensor& x_in, const at::Tensor& w_in, const std:
   at::Tensor x = as_rows(x_in, rows, K);
   if (!rows_ok(x)) x = x.contiguous();
   at::Tensor w = rows_ok(w_in) ? w_in : w_in.contiguous();
-  at::Tensor bias;
-  if (bias_opt.has_value() && bias_opt->defined()) {
+  const bool gated = mul_opt.has_value() && mul_opt->defined();
+  at::Tensor bias, mul;
+  if (gated) {
+    // out = act(x W^T) * mul: the gated form takes no bias.
+    require_cuda(*mul_opt, "mul");
+    TORCH_CHECK(!(bias_opt.has_value() && bias_opt->defined()), "vf_b200: the gated form (mul) takes no bias");
+    TORCH_CHECK(mul_opt->scalar_type() == x.scalar_type(), "vf_b200: mul must have x's dtype");
+    TORCH_CHECK(mul_opt->numel() == rows * N && mul_opt->size(-1) == N, "vf_b200: mul must be [..., out_features] like the result");
+    mul = as_rows(*mul_opt, rows, N);
+    if (!rows_ok(mul)) mul = mul.contiguous();
+  } else if (bias_opt.has_value() && bias_opt->defined()) {
     require_cuda(*bias_opt, "bias");
     TORCH_CHECK(bias_opt->dim() == 1 && bias_opt->size(0) == N, "vf_b200: bias must be [out_features]");
     bias = bias_opt->to(x.scalar_type()).contiguous();
@@ -579,7 +588,9 @@ at::Tensor linear_act(const at::Tensor& x_in, const at::Tensor& w_in, const std:
   a.dtype = dtype_code(x);
   a.x = x.data_ptr();
   a.weight = w.data_ptr();
-  a.bias = bias.data_ptr();
+  a.bias = gated ? nullptr : bias.data_ptr();
+  a.mul = gated ? mul.data_ptr() : nullptr;
+  a.mul_row_stride = gated ? (rows > 1 ? mul.stride(0) : N) : 0;
   a.out = out.data_ptr();
   a.rows = rows;
   a.K = K;
@@ -591,12 +602,14 @@ at::Tensor linear_act(const at::Tensor& x_in, const at::Tensor& w_in, const std:
   check_rc(vf_linear_act_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
   return out;
 }
-at::Tensor linear_act_meta(const at::Tensor& x, const at::Tensor& w, const std::optional<at::Tensor>&, int64_t) {
+at::Tensor linear_act_meta(const at::Tensor& x, const at::Tensor& w, const std::optional<at::Tensor>&,
+                           const std::optional<at::Tensor>&, int64_t) {
   std::vector<int64_t> out_shape(x.sizes().begin(), x.sizes().end());
   out_shape.back() = w.size(0);
   return at::empty(out_shape, x.options());
 }
-at::Tensor linear_act_cpu(const at::Tensor&, const at::Tensor&, const std::optional<at::Tensor>&, int64_t) {
+at::Tensor linear_act_cpu(const at::Tensor&, const at::Tensor&, const std::optional<at::Tensor>&,
+                          const std::optional<at::Tensor>&, int64_t) {
   TORCH_CHECK(false, "vf_b200: x and weight must be CUDA tensors (no CPU implementation)");
 }
 
@@ -760,7 +773,7 @@ TORCH_LIBRARY(vf_b200, m) {
   m.def("deberta_attention_fused_varlen(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, int max_seqlen, "
         "Tensor? rel_key, Tensor? rel_query, bool causal, float? sm_scale, int position_buckets, "
         "int max_relative_distance, bool use_log_bucket) -> Tensor");
-  m.def("linear_act(Tensor x, Tensor weight, Tensor? bias, int act) -> Tensor");
+  m.def("linear_act(Tensor x, Tensor weight, Tensor? bias, Tensor? mul, int act) -> Tensor");
   m.def("span_scores(Tensor start_proj, Tensor end_proj, Tensor span_idx, Tensor classes, Tensor? class_bias, "
         "int[] word_offsets, int[] span_offsets, int[] class_offsets, ScalarType out_dtype) -> Tensor");
 }

@@ -1,6 +1,7 @@
-"""Linear + exact GELU with the activation in the GEMM's epilogue — the DeBERTa feed-forward's
+"""Linear + activation with the activation in the GEMM's epilogue — the DeBERTa feed-forward's
 first half, models/deberta_v2/deberta_v2_encoder.py:547-550 (DebertaV2Intermediate.forward:
-`self.dense(hidden_states)`, then ACT2FN["gelu"], torch's exact GELU).
+`self.dense(hidden_states)`, then ACT2FN["gelu"], torch's exact GELU), and the mT5 gated
+activation (`gated_gelu_tanh`, below).
 
 The reference writes the [tokens, intermediate_size] product to HBM and reads it back for the
 activation; `linear_gelu` runs one sm_100a GEMM (csrc/vf_gemm.cu: CUTLASS sm100 templates,
@@ -16,13 +17,22 @@ import torch
 
 import vf_b200.ops  # noqa: F401  (loads the kernels and registers torch.ops.vf_b200)
 
-ACT_GELU_ERF = 1   # VF_ACT_GELU_ERF
+ACT_GELU_TANH, ACT_GELU_ERF = 0, 1   # VF_ACT_GELU_TANH, VF_ACT_GELU_ERF
 
 
 def linear_gelu(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     """F.gelu(F.linear(x, weight, bias)) (exact GELU) as one GEMM; x [..., K] 16-bit, weight
     [N, K] (nn.Linear layout), bias [N] or None; K and N multiples of 8."""
-    return torch.ops.vf_b200.linear_act(x, weight, bias, ACT_GELU_ERF)
+    return torch.ops.vf_b200.linear_act(x, weight, bias, None, ACT_GELU_ERF)
+
+
+def gated_gelu_tanh(x: torch.Tensor, gate_weight: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """The mT5 gated feed-forward activation with the gate projection as its GEMM:
+    gelu_tanh(x gate_weight^T) * up (the reference's fused_gelu_mul_dropout(wi_0(x), wi_1(x),
+    "gelu_new") at models/mt5/mt5_encoder.py:427-437), `up` = wi_1(x) computed by the caller;
+    the activation and the product run in the epilogue, so the gate projection never reaches
+    HBM.  x [..., K], gate_weight [N, K], up [..., N], one 16-bit dtype."""
+    return torch.ops.vf_b200.linear_act(x, gate_weight, None, up, ACT_GELU_TANH)
 
 
 def _exact_gelu(act_fn) -> bool:
@@ -63,4 +73,4 @@ def install_fused_intermediate(intermediate_cls) -> None:
     intermediate_cls.forward = deberta_intermediate_forward
 
 
-__all__ = ["linear_gelu", "deberta_intermediate_forward", "install_fused_intermediate"]
+__all__ = ["linear_gelu", "gated_gelu_tanh", "deberta_intermediate_forward", "install_fused_intermediate"]

@@ -120,12 +120,14 @@ class LinearActArgs(ctypes.Structure):
         ("x", ctypes.c_void_p),
         ("weight", ctypes.c_void_p),
         ("bias", ctypes.c_void_p),
+        ("mul", ctypes.c_void_p),
         ("out", ctypes.c_void_p),
         ("rows", ctypes.c_int64),
         ("K", ctypes.c_int64),
         ("N", ctypes.c_int64),
         ("x_row_stride", ctypes.c_int64),
         ("weight_row_stride", ctypes.c_int64),
+        ("mul_row_stride", ctypes.c_int64),
         ("out_row_stride", ctypes.c_int64),
         ("act", ctypes.c_int32),
     ]

@@ -179,7 +179,7 @@ class MT5Encoder:
     same signatures)."""
 
     def __init__(self, cfg: MT5Config = MT5Config(), device="cuda", dtype=torch.bfloat16, seed: int = 0,
-                 attention_fn=None, gated_act=None):
+                 attention_fn=None, gated_act=None, fused_ffn: Optional[bool] = None):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         g = torch.Generator(device=self.device).manual_seed(seed)
         E, F_ = cfg.hidden, cfg.ffn
@@ -196,9 +196,15 @@ class MT5Encoder:
         if attention_fn is None:
             from kernels.flash_attention_rpb import flash_attention_rpb_varlen as attention_fn
         self.attention_fn = attention_fn
+        # The gated-GELU in the gate projection's GEMM epilogue (kernels.linear_act), unless
+        # another activation function was given: up = x wi_1^T, then gelu_tanh(x wi_0^T) * up.
+        self.fused_ffn = (gated_act is None) if fused_ffn is None else fused_ffn
         if gated_act is None:
             from kernels.ff_fused import fused_gelu_mul_dropout as gated_act
         self.gated_act = gated_act
+        if self.fused_ffn:
+            from kernels.linear_act import gated_gelu_tanh
+            self.gated_gelu_tanh = gated_gelu_tanh
 
     @torch.no_grad()
     def forward(self, ids: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
@@ -212,8 +218,12 @@ class MT5Encoder:
                                     cfg.num_buckets, cfg.max_distance, False, 1.0)
             h = h + ctx.reshape(T, E).to(h.dtype) @ L["wo"].t()
             x = _rms_norm(h, L["ln2"], cfg.eps)
-            gu = x @ L["wi"].t()
-            f = self.gated_act(gu[:, :F_], gu[:, F_:], "gelu_new")     # gated-GELU, halves read in place
+            if self.fused_ffn:
+                up = x @ L["wi"][F_:].t()
+                f = self.gated_gelu_tanh(x, L["wi"][:F_], up)
+            else:
+                gu = x @ L["wi"].t()
+                f = self.gated_act(gu[:, :F_], gu[:, F_:], "gelu_new")     # gated-GELU, halves read in place
             h = h + f @ L["wo_ff"].t()
         return _rms_norm(h, self.final_ln, cfg.eps)
 
