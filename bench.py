@@ -86,9 +86,14 @@ def pipelined_e2e(dev, host: dict, call, n_steps: int, world: int):
     cur = torch.cuda.current_stream(dev)
     up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     keys = [k for k, v in host.items() if isinstance(v, torch.Tensor)]
-    slots = [{k: torch.empty(host[k].shape, dtype=host[k].dtype, device=dev) for k in keys} for _ in range(2)]
+    # Device slots and pinned outputs take the strides of their source (the DeBERTa inputs are
+    # permuted views of a projection, as the reference's caller builds them), so each copy is
+    # one asynchronous memcpy of the dense block, not a host-side transpose through pageable
+    # memory.
+    slots = [{k: torch.empty_strided(host[k].size(), host[k].stride(), dtype=host[k].dtype, device=dev)
+              for k in keys} for _ in range(2)]
     probe = call({**host, **{k: slots[0][k].copy_(host[k]) for k in keys}})
-    outs = [torch.empty(probe.shape, dtype=probe.dtype).pin_memory() for _ in range(2)]
+    outs = [torch.empty_strided(probe.size(), probe.stride(), dtype=probe.dtype, pin_memory=True) for _ in range(2)]
     torch.cuda.synchronize()
     h2d = sum(host[k].numel() * host[k].element_size() for k in keys)
     d2h = outs[0].numel() * outs[0].element_size()
@@ -740,6 +745,58 @@ def run_gliner_span(args, world: int, rank: int, dev, warmup: int):
             **({"cpu_baseline": gliner_span_cpu_baseline()} if world == 1 and not args.no_cpu_baseline else {})}
 
 
+def run_gliner_span_reference_gpu(args, dev, warmup: int):
+    """The reference's own span head on this GPU (--impl reference_triton --workload gliner_span):
+    poolers/gliner.py's SpanMarkerV0 from the reference install with this workload's weights,
+    then the pooler's einsum (:285-289), one request at a time as GLiNERSpanPooler.forward loops,
+    bf16, on the same batches.  A secondary bar beside the CPU reference arm."""
+    import importlib.util
+    from vf_b200 import workloads as W
+    ref = Path(os.environ.get("VF_REFERENCE", str(ROOT / "baseline" / "_ref")))
+    path = ref / "poolers" / "gliner.py"
+    if not path.exists():
+        return {"impl": "reference_triton", "unavailable": f"no reference install at {ref}"}
+    if str(ref) not in sys.path:
+        sys.path.append(str(ref))                  # vllm_factory.pooling, imported by the pooler
+    spec = importlib.util.spec_from_file_location("_vf_reference_gliner_pooler", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    ours = W.gliner_span_marker(device=dev)
+    marker = mod.SpanMarkerV0(W.SPAN_HIDDEN, W.SPAN_MAX_WIDTH, dropout=0.0)
+    with torch.no_grad():
+        for (na, a), (nb, b) in zip(marker.named_parameters(), ours.named_parameters()):
+            assert na == nb and a.shape == b.shape, (na, nb)
+            a.copy_(b.float())
+    marker = marker.to(device=dev, dtype=torch.bfloat16).eval()
+    sets = [W.gliner_span_batch(seed=6100 + i, device=dev) for i in range(4)]
+
+    def step(b):
+        wo, so, co = b["word_offsets"], b["span_offsets"], b["class_offsets"]
+        for g in range(len(wo) - 1):
+            rep = marker(b["words"][wo[g]:wo[g + 1]][None], b["span_idx"][so[g]:so[g + 1]][None])
+            torch.einsum("BLKD,BCD->BLKC", rep, b["classes"][co[g]:co[g + 1]][None])
+
+    stream = torch.cuda.current_stream(dev)
+    steps = max(3, min(args.steps, 10))
+    with torch.no_grad():
+        for i in range(warmup):
+            step(sets[i % len(sets)])
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for i in range(steps):
+            step(sets[i % len(sets)])
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    spans = float(sum(sets[i % len(sets)]["span_offsets"][-1] for i in range(steps)))
+    return {"metric": METRIC, "value": spans / (ms * 1e-3), "unit": "spans/s", "n_gpus": 1, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference_triton",
+            "config": GLINER_SPAN_CONFIG,
+            "what": "the reference's SpanMarkerV0 + einsum (torch, bf16) on this GPU, one request at a time"}
+
+
 # ----------------------------------------------------------------------------- attention lines
 def reference_triton_kernels():
     """The reference's own Triton modules (kernels/flash_attention_rpb.py,
@@ -942,6 +999,9 @@ def main():
             return
         import vf_b200
         vf_b200.load()                  # the input generators share this repository's workloads
+        if headline == "gliner_span":
+            print(json.dumps(run_gliner_span_reference_gpu(args, dev, warmup)))
+            return
         line = run_attention(args, headline, args.steps, 1, 0, dev, warmup, False, impl="reference_triton")
         if subs:
             line["sub_results"] = {

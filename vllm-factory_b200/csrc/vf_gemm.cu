@@ -6,10 +6,11 @@
 // an elementwise pass that reads it back and writes it again.  Here the activation runs in the
 // GEMM's epilogue, on the fp32 accumulator in registers, so the intermediate never exists.
 //
-// The GEMM is a CUTLASS 3.x sm100 kernel instantiated in this file (CuTe / CUTLASS templates;
+// The GEMMs are CUTLASS 3.x sm100 kernels instantiated in this file (CuTe / CUTLASS templates;
 // the headers come from the CUTLASS tree found at build time): tcgen05 UMMA with a TMEM
-// accumulator, 128 x 256 x 64 tiles on one SM (no cluster, so every TMA load is a plain
-// single-CTA load: nothing here multicasts), a TMA-store epilogue with the per-column bias and
+// accumulator, 256 x 256 x 64 tiles on SM pairs (cluster 2 x 1 x 1; CUTLASS's builder gives a
+// cluster whose N extent is 1 the 2-SM TMA load without multicast, and no load in this file
+// multicasts), a TMA-store epilogue with the per-column bias and
 // cutlass::epilogue::thread::GELU (0.5 x (1 + erf(x / sqrt 2)), the formula of torch's
 // exact GELU) in fp32 before the rounding to the output dtype.
 #include <cuda.h>
@@ -38,23 +39,41 @@ namespace gemm {
 
 using namespace cute;
 
+// Tile and schedule shared by both forms: a 256 x 256 x 64 tile on a pair of SMs
+// (tcgen05 cta_group::2, cluster 2 x 1 x 1; each SM of the pair loads its own half of A and
+// of B, so the pair's TMA loads are 2-SM loads without multicast), or 128 x 256 x 64 on one SM.
+#ifndef VF_GEMM_2SM
+#define VF_GEMM_2SM 1
+#endif
+#if VF_GEMM_2SM
+using TileShape = Shape<_256, _256, _64>;
+using ClusterShape = Shape<_2, _1, _1>;
+using EpilogueSchedule = cutlass::epilogue::TmaWarpSpecialized2Sm;
+using MainloopSchedule = cutlass::gemm::KernelTmaWarpSpecialized2SmSm100;
+#else
+using TileShape = Shape<_128, _256, _64>;
+using ClusterShape = Shape<_1, _1, _1>;
+using EpilogueSchedule = cutlass::epilogue::TmaWarpSpecialized1Sm;
+using MainloopSchedule = cutlass::gemm::KernelTmaWarpSpecialized1SmSm100;
+#endif
+
 // D[M, N] = GELU(A[M, K] B[K, N] + bias[N]); A = x (row-major, K contiguous), B = W^T with W
 // the [N, K] nn.Linear weight (column-major B), D row-major.
 template <typename E>
 struct LinearGelu {
-  using MmaTile = Shape<_128, _256, _64>;
-  using Cluster = Shape<_1, _1, _1>;
+  using MmaTile = TileShape;
+  using Cluster = ClusterShape;
   using Fusion = cutlass::epilogue::fusion::LinCombPerColBiasEltAct<cutlass::epilogue::thread::GELU, E, float, E, E,
                                                                     float>;
   using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
       cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, MmaTile, Cluster,
       cutlass::epilogue::collective::EpilogueTileAuto, float, float, void, cutlass::layout::RowMajor, 8, E,
-      cutlass::layout::RowMajor, 8, cutlass::epilogue::TmaWarpSpecialized1Sm, Fusion>::CollectiveOp;
+      cutlass::layout::RowMajor, 8, EpilogueSchedule, Fusion>::CollectiveOp;
   using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
       cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, E, cutlass::layout::RowMajor, 8, E,
       cutlass::layout::ColumnMajor, 8, float, MmaTile, Cluster,
       cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename Epilogue::SharedStorage))>,
-      cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;
+      MainloopSchedule>::CollectiveOp;
   using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue, void>;
   using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
 };
@@ -66,8 +85,8 @@ struct LinearGelu {
 // reference kernel, with the tanh.approx instruction) of the accumulator, times the source C.
 template <typename E>
 struct LinearGeluTanhMul {
-  using MmaTile = Shape<_128, _256, _64>;
-  using Cluster = Shape<_1, _1, _1>;
+  using MmaTile = TileShape;
+  using Cluster = ClusterShape;
   static constexpr auto RS = cutlass::FloatRoundStyle::round_to_nearest;
   using Act = cutlass::epilogue::fusion::Sm90EVT<
       cutlass::epilogue::fusion::Sm90Compute<cutlass::epilogue::thread::GELU_taylor, float, float, RS>,
@@ -78,12 +97,12 @@ struct LinearGeluTanhMul {
   using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
       cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, MmaTile, Cluster,
       cutlass::epilogue::collective::EpilogueTileAuto, float, float, E, cutlass::layout::RowMajor, 8, E,
-      cutlass::layout::RowMajor, 8, cutlass::epilogue::TmaWarpSpecialized1Sm, Fusion>::CollectiveOp;
+      cutlass::layout::RowMajor, 8, EpilogueSchedule, Fusion>::CollectiveOp;
   using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
       cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, E, cutlass::layout::RowMajor, 8, E,
       cutlass::layout::ColumnMajor, 8, float, MmaTile, Cluster,
       cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename Epilogue::SharedStorage))>,
-      cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;
+      MainloopSchedule>::CollectiveOp;
   using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue, void>;
   using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
 };

@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) span_scores_kernel(const
   uint64_t* done = empty + kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* rng = reinterpret_cast<int*>(tmem_slot + 2);     // i_min, i_max, j_min, j_max
+  int* rng = reinterpret_cast<int*>(tmem_slot + 2);     // i_min, i_max, j_min, j_max over rows with i, j > 0
 
   // This CTA's segment: the last g with tile_off[g] <= tile (segments without tiles have
   // tile_off[g] == tile_off[g + 1] and are passed over).
@@ -169,50 +169,56 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks) span_scores_kernel(const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Word 0 is left out of the ranges: masked spans are (0, 0) (the pooler multiplies span_idx by
+  // the span mask), and the last tiles of a sentence hold them beside its last words.
   if (warp < 4) {
-    atomicMin(&rng[0], i);
-    atomicMax(&rng[1], i);
-    atomicMin(&rng[2], j);
-    atomicMax(&rng[3], j);
+    if (i > 0) { atomicMin(&rng[0], i); atomicMax(&rng[1], i); }
+    if (j > 0) { atomicMin(&rng[2], j); atomicMax(&rng[3], j); }
   }
   __syncthreads();
-  // Staged tile: its start words and its end words each lie within kRowBox consecutive rows (the
-  // reference's default enumeration gives <= ceil(128 / max_width) + 1 and that + max_width - 1),
-  // so every stage brings them in as two TMA boxes; otherwise each thread loads its own rows.
-  const int i_min = rng[0], j_min = rng[2];
-  const bool staged = rng[1] - i_min < kRowBox && rng[3] - j_min < kRowBox;
+  // Staged tile: its start words and its end words other than word 0 each lie within kRowBox
+  // consecutive rows (the reference's default enumeration gives <= ceil(128 / max_width) + 1
+  // and that + max_width - 1), so every stage brings them in as two TMA boxes, and a row
+  // outside its box (word 0) is loaded by its own thread; otherwise each thread loads its own
+  // rows.  (No row > 0: the boxes start at word 0.)
+  const int i_min = rng[1] < 0 ? 0 : rng[0], j_min = rng[3] < 0 ? 0 : rng[2];
+  const bool staged = (rng[1] < 0 || rng[1] - i_min < kRowBox) && (rng[3] < 0 || rng[3] - j_min < kRowBox);
 
   if (warp < 4) {
     // ---------------------------------------------------------------- A rows + epilogue
     const uint4* ur = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.u) + (p.word_off[g] + (long long)i) * p.us);
     const uint4* vr = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.v) + (p.word_off[g] + (long long)j) * p.vs);
     const uint32_t ru = static_cast<uint32_t>(i - i_min), rv = static_cast<uint32_t>(j - j_min);   // rows in the boxes
+    const bool u_box = staged && ru < static_cast<uint32_t>(kRowBox);   // (i < i_min wraps above kRowBox)
+    const bool v_box = staged && rv < static_cast<uint32_t>(kRowBox);
+    // Each row is read through a generic pointer: its box row in shared memory (16-byte chunk q
+    // at q ^ (row & 7), the 128-byte swizzle; the base moves by stage) or its row in global
+    // memory (chunk q at q; the base moves by 64 columns a stage).
+    const uint8_t* ubase = u_box ? sU + ru * 128 : reinterpret_cast<const uint8_t*>(ur);
+    const uint8_t* vbase = v_box ? sV + rv * 128 : reinterpret_cast<const uint8_t*>(vr);
+    const uint32_t usw = u_box ? (ru & 7u) : 0u, vsw = v_box ? (rv & 7u) : 0u;
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;   // this warp's TMEM lanes
     bool ok = true;
     for (int kc = 0; kc < nk; ++kc) {
       const int st = kc % kStages;
-      uint4 a[8], b[8];
       if (staged) {
+        // The stage's boxes have landed; its TMEM columns are free too (the TMA refilled the
+        // stage only after the MMAs that read it had completed).
         ok = mbar_wait(&full_b[st], (kc / kStages) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-        const uint8_t* urow = sU + st * kBoxBytes + ru * 128;
-        const uint8_t* vrow = sV + st * kBoxBytes + rv * 128;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {   // 16-byte chunk q of a row sits at q ^ (row & 7) (128-byte swizzle)
-          a[q] = *reinterpret_cast<const uint4*>(urow + ((static_cast<uint32_t>(q) ^ (ru & 7u)) << 4));
-          b[q] = *reinterpret_cast<const uint4*>(vrow + ((static_cast<uint32_t>(q) ^ (rv & 7u)) << 4));
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          a[q] = __ldg(ur + kc * 8 + q);
-          b[q] = __ldg(vr + kc * 8 + q);
-        }
-      }
-      if (kc >= kStages) {
+        tc_fence_after();
+      } else if (kc >= kStages) {
         ok = mbar_wait(&empty[st], ((kc / kStages) - 1) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
+      }
+      const uint8_t* up = ubase + (u_box ? st * kBoxBytes : kc * 128);
+      const uint8_t* vp = vbase + (v_box ? st * kBoxBytes : kc * 128);
+      uint4 a[8], b[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        a[q] = *reinterpret_cast<const uint4*>(up + ((static_cast<uint32_t>(q) ^ usw) << 4));
+        b[q] = *reinterpret_cast<const uint4*>(vp + ((static_cast<uint32_t>(q) ^ vsw) << 4));
       }
       // Row t of the A stage: 64 elements as 32 packed pairs, K in column order.
       uint32_t r[32];
