@@ -18,7 +18,7 @@ INCLUDE = PKG_DIR.parent.parent / "include"
 LIB_PATH = PKG_DIR / "libvf_b200.so"
 TORCH_LIB_PATH = PKG_DIR / "libvf_b200_torch.so"
 SOURCES = [CSRC / "vf_attention.cu", CSRC / "vf_deberta_fused.cu", CSRC / "vf_ffn.cu", CSRC / "vf_layernorm.cu",
-           CSRC / "vf_span.cu", CSRC / "vf_gemm.cu"]
+           CSRC / "vf_span.cu"]
 DEPS = SOURCES + [CSRC / "vf_ptx.cuh", CSRC / "vf_internal.h", INCLUDE / "vf_b200.h"]
 TORCH_SOURCES = [CSRC / "vf_torch_ops.cpp"]
 TORCH_DEPS = TORCH_SOURCES + [INCLUDE / "vf_b200.h"]
@@ -29,26 +29,6 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC,-O2,-fvisibility=hidden",
     "-shared",
 ]
-
-
-def cutlass_root() -> Path:
-    """A CUTLASS source tree (include/cutlass, include/cute, tools/util/include) for the
-    templates vf_gemm.cu instantiates: $VF_CUTLASS_DIR, else the copy shipped inside an
-    installed Python package (flashinfer's or tilelang's)."""
-    cands = [os.environ.get("VF_CUTLASS_DIR")]
-    for mod, sub in (("flashinfer", "data/cutlass"), ("tilelang", "3rdparty/cutlass")):
-        try:
-            import importlib.util
-            spec = importlib.util.find_spec(mod)
-        except (ImportError, ValueError):
-            spec = None
-        if spec is not None and spec.submodule_search_locations:
-            cands.append(str(Path(list(spec.submodule_search_locations)[0]) / sub))
-    for c in cands:
-        if c and (Path(c) / "include" / "cutlass" / "cutlass.h").exists() and \
-                (Path(c) / "tools" / "util" / "include" / "cutlass" / "util" / "packed_stride.hpp").exists():
-            return Path(c)
-    raise RuntimeError("no CUTLASS tree found for vf_gemm.cu (set VF_CUTLASS_DIR to a CUTLASS checkout)")
 
 
 def nvcc_path() -> str:
@@ -137,10 +117,7 @@ def build_kernels(force: bool = False, verbose: bool = False) -> Path:
     if not force and not _stale(LIB_PATH, DEPS):
         return LIB_PATH
     tmp = LIB_PATH.with_suffix(".so.tmp")
-    cut = cutlass_root()
-    cmd = [nvcc_path(), *NVCC_FLAGS, "--expt-relaxed-constexpr", "-diag-suppress", "20012", "-I", str(INCLUDE),
-           "-I", str(cut / "include"), "-I", str(cut / "tools" / "util" / "include"), "-o", str(tmp),
-           *map(str, SOURCES)]
+    cmd = [nvcc_path(), *NVCC_FLAGS, "-I", str(INCLUDE), "-o", str(tmp), *map(str, SOURCES)]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), file=sys.stderr)
