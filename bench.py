@@ -31,8 +31,9 @@ one GPU on the same input sets (a secondary bar beside the CPU reference arm).
 Named workloads (`--workload`): mt5_c2, mt5_c2_varlen, deberta_c1[_fused], deberta_c1_fp32,
 deberta_c1_varlen[_fused], deberta_c5_<L>[_fused] (L = 1024, 2048, 4096), the encoder
 stacks deberta_c3 / mt5_c4, the HBM-bound ops beside the path, mt5_ffn_act /
-deberta_add_ln (value = GB/s), and the GLiNER span head downstream of the encoder,
-gliner_span (value = spans/s).
+deberta_add_ln (value = GB/s), the feed-forward GEMMs with the activation in the
+epilogue, deberta_ffn_gemm / mt5_ffn_gemm (TFLOP/s), and the GLiNER span head downstream
+of the encoder, gliner_span (value = spans/s).
 """
 from __future__ import annotations
 
@@ -540,13 +541,16 @@ def add_layer_norm_cpu_baseline(budget_s: float = 10.0):
             "kind": "port", "sample": f"{n} x 2048 rows of the 65536 x 1024 workload, float64 torch on CPU (oracle)"}
 
 
-def _run_hbm_op(args, world: int, rank: int, dev, warmup: int, sets, call, nbytes: int, cfg: dict, cpu_fn):
-    """Shared timing of the HBM-bound elementwise ops: `call(*sets[i % len(sets)])` per
-    step; value = algorithmic bytes / time (GB/s).  The host time of one op call (Python,
-    dispatch, output allocation) exceeds these kernels' device time, so the K timed steps
-    are captured once in a CUDA graph and the replay is timed: all K launches run, back to
-    back.  e2e: eager calls, the first input set from pinned host memory in, the result
-    out, every step."""
+def _run_hbm_op(args, world: int, rank: int, dev, warmup: int, sets, call, nbytes: int, cfg: dict, cpu_fn,
+                bound: str = "hbm"):
+    """Shared timing of the ops beside the path: `call(*sets[i % len(sets)])` per step.
+    bound "hbm": value = algorithmic bytes (`nbytes`) / time in GB/s against the measured
+    HBM copy; bound "tensor": `nbytes` holds the algorithmic FLOPs, value in TFLOP/s against
+    the measured bf16 GEMM peak.  The host time of one op call (Python, dispatch, output
+    allocation) exceeds the elementwise kernels' device time, so the K timed steps are
+    captured once in a CUDA graph and the replay is timed: all K launches run, back to back.
+    e2e: eager calls, the first input set from pinned host memory in, the result out, every
+    step."""
     stream = torch.cuda.current_stream(dev)
     for i in range(warmup):
         call(*sets[i % len(sets)])
@@ -571,24 +575,29 @@ def _run_hbm_op(args, world: int, rank: int, dev, warmup: int, sets, call, nbyte
     ms = ev0.elapsed_time(ev1)
     from vf_b200 import dist as VD
     ms_max, bytes_all, _ = VD.reduce_timing(ms, float(nbytes), 0.0, dev)
-    value = bytes_all * args.steps / (ms_max * 1e-3) / 1e9
+    div, unit = (1e9, "GB/s") if bound == "hbm" else (1e12, "TFLOP/s")
+    value = bytes_all * args.steps / (ms_max * 1e-3) / div
     e2e = None
     if not args.no_e2e:
         host = {str(j): t.cpu().pin_memory() for j, t in enumerate(sets[0])}
         n_e2e = max(3, min(args.steps, 10))
         ems, h2d, d2h = pipelined_e2e(dev, host, lambda x: call(*(x[str(j)] for j in range(len(host)))), n_e2e, world)
-        e2e = {"value": bytes_all * n_e2e / (ems * 1e-3) / 1e9, "unit": "GB/s", "pipelined": True,
+        e2e = {"value": bytes_all * n_e2e / (ems * 1e-3) / div, "unit": unit, "pipelined": True,
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": n_e2e}
     if rank != 0:
         return None
     peaks = measured_peaks()
-    achieved = nbytes / (ms / args.steps * 1e-3) / 1e9
-    return {"metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+    achieved = nbytes / (ms / args.steps * 1e-3) / div
+    if bound == "hbm":
+        peak, src, work = peaks.get("hbm", 6650.0), f"{peaks['source']} HBM copy", "algorithmic_bytes_per_launch"
+    else:
+        peak, src, work = peaks["bf16"], f"{peaks['source']} bf16 GEMM (burst)", "algorithmic_flops_per_launch"
+    return {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks.get("hbm", 6650.0), "unit": "GB/s",
-                         "frac": achieved / peaks.get("hbm", 6650.0), "traffic": committed_traffic(args.workload),
-                         "peak_source": f"{peaks['source']} HBM copy", "algorithmic_bytes_per_launch": nbytes},
+            "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                         "frac": achieved / peak, "traffic": committed_traffic(args.workload),
+                         "peak_source": src, work: nbytes},
             "gpu_launches": args.steps, "clocks": clocks, "e2e": e2e,
             **({"cpu_baseline": cpu_fn()} if world == 1 and not args.no_cpu_baseline else {})}
 
@@ -622,6 +631,66 @@ def run_add_layer_norm(args, world: int, rank: int, dev, warmup: int):
     cfg = {"workload": "DeBERTa-v3-large residual add + LayerNorm (kernels/fused_add_layernorm.py), 65536 x 1024",
            "l2": "2 rotating 256 MB input sets > L2; no flush", "launch": "K steps in one CUDA graph"}
     return _run_hbm_op(args, world, rank, dev, warmup, sets, call, 3 * T * E * 2, cfg, add_layer_norm_cpu_baseline)
+
+
+FFN_GEMM_SHAPES = {"deberta_ffn_gemm": (65536, 1024, 4096), "mt5_ffn_gemm": (65536, 1024, 2816)}
+
+
+def ffn_gemm_cpu_baseline(name: str, budget_s: float = 10.0):
+    """The oracle's unfused arithmetic (float64 torch: projection, then the activation) on
+    the host cores over a 256-row slice of the workload, repeated for ~10 s: TFLOP/s of the
+    same GEMM work."""
+    import oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    M, K, N = FFN_GEMM_SHAPES[name]
+    rows = 256
+    g = torch.Generator().manual_seed(6000)
+    x = torch.randn(rows, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g) * 0.03).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+    up = torch.randn(rows, N, generator=g).to(torch.bfloat16)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        if name == "deberta_ffn_gemm":
+            oracle.linear_gelu_ref(x, w, b)
+        else:
+            oracle.gated_act_ref(x.double() @ w.double().t(), up, 0)   # 0: GELU_tanh (oracle/ffn.py)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n * 2.0 * rows * N * K / dt / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{n} x {rows} rows of the {M} x {N} x {K} workload, float64 torch on CPU (oracle)"}
+
+
+def ffn_gemm_config(name: str) -> dict:
+    M, K, N = FFN_GEMM_SHAPES[name]
+    what = ("DeBERTa-v3-large FFN dense + exact GELU (kernels/linear_act.py linear_gelu)" if name == "deberta_ffn_gemm"
+            else "mT5-large gate projection x GELU_tanh x up (kernels/linear_act.py gated_gelu_tanh)")
+    return {"workload": f"{what}, {M} x {K} -> {N}, bf16",
+            "l2": "2 rotating input sets (x 128 MB, outputs 368-512 MB) > L2; no flush",
+            "launch": "K steps in one CUDA graph"}
+
+
+def run_ffn_gemm(args, world: int, rank: int, dev, warmup: int):
+    """deberta_ffn_gemm: GELU(x W^T + b), the DeBERTa-v3-large feed-forward's first half
+    (kernels.linear_act.linear_gelu, DebertaV2Intermediate), 65536 tokens x 1024 -> 4096.
+    mt5_ffn_gemm: GELU_tanh(x wi_0^T) * up, the mT5-large gate projection with the gated
+    activation in its epilogue (kernels.linear_act.gated_gelu_tanh), 65536 x 1024 -> 2816.
+    Tensor-bound: value = 2 M N K / time, TFLOP/s."""
+    from kernels.linear_act import gated_gelu_tanh, linear_gelu
+    name = args.workload
+    M, K, N = FFN_GEMM_SHAPES[name]
+    g = torch.Generator(device=dev).manual_seed(6000 + rank)
+    w = (torch.randn(N, K, generator=g, device=dev) * 0.03).to(torch.bfloat16)
+    if name == "deberta_ffn_gemm":
+        b = (torch.randn(N, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        sets = [(torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16),) for _ in range(2)]
+        call = lambda x: linear_gelu(x, w, b)
+    else:
+        sets = [(torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16),
+                 torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16)) for _ in range(2)]
+        call = lambda x, up: gated_gelu_tanh(x, w, up)
+    return _run_hbm_op(args, world, rank, dev, warmup, sets, call, 2 * M * N * K, ffn_gemm_config(name),
+                       lambda: ffn_gemm_cpu_baseline(name), bound="tensor")
 
 
 # ----------------------------------------------------------------------------- GLiNER span head
@@ -943,6 +1012,8 @@ def reference_line(args, name: str) -> dict:
         cb, cfg = gated_act_cpu_baseline(), {"workload": name}
     elif name == "deberta_add_ln":
         cb, cfg = add_layer_norm_cpu_baseline(), {"workload": name}
+    elif name in FFN_GEMM_SHAPES:
+        cb, cfg = ffn_gemm_cpu_baseline(name), ffn_gemm_config(name)
     elif name == "gliner_span":
         cb, cfg = gliner_span_cpu_baseline(), GLINER_SPAN_CONFIG
     else:
@@ -1029,6 +1100,8 @@ def main():
         line = run_gated_act(args, world, rank, dev, warmup)
     elif headline == "deberta_add_ln":
         line = run_add_layer_norm(args, world, rank, dev, warmup)
+    elif headline in FFN_GEMM_SHAPES:
+        line = run_ffn_gemm(args, world, rank, dev, warmup)
     elif headline == "gliner_span":
         line = run_gliner_span(args, world, rank, dev, warmup)
     else:

@@ -237,6 +237,36 @@ typedef struct {
 int vf_gated_act_fwd(const vf_gated_act_args_t* args, void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * Linear + activation of the encoder feed-forwards, the activation applied to the fp32
+ * accumulator in the GEMM's epilogue.  Replaces
+ * models/deberta_v2/deberta_v2_encoder.py:547-550 (DebertaV2Intermediate.forward:
+ * `self.dense(hidden_states)` then `self.intermediate_act_fn`, ACT2FN["gelu"] = exact GELU),
+ * two torch calls with the [rows, N] intermediate in HBM between them.
+ * x: [rows, K], weight: [N, K] (nn.Linear layout), bias: [N] (required), out: [rows, N];
+ * one 16-bit dtype, unit column strides, row strides in elements; K, N and every row stride
+ * multiples of 8, pointers 16-byte aligned; out must not overlap the inputs.  Built forms:
+ *  - act = VF_ACT_GELU_ERF, bias given, mul = NULL: out = GELU(x W^T + bias), GELU the exact
+ *    0.5 z (1 + erf(z / sqrt 2));
+ *  - act = VF_ACT_GELU_TANH, bias = NULL, mul given: out = GELU_tanh(x W^T) * mul, the gated
+ *    activation of the mT5 feed-forward (models/mt5/mt5_encoder.py:427-437 calling
+ *    kernels/ff_fused.py:86 with "gelu_new"): W = wi_0 (gate), mul = x wi_1^T (up, [rows, N],
+ *    row stride mul_row_stride), replacing the stacked projection + vf_gated_act_fwd pass.
+ * ------------------------------------------------------------------------------------ */
+typedef struct {
+  vf_dtype_t dtype;
+  const void* x;
+  const void* weight;
+  const void* bias;
+  const void* mul;
+  void* out;
+  int64_t rows, K, N;
+  int64_t x_row_stride, weight_row_stride, mul_row_stride, out_row_stride;
+  int32_t act;
+} vf_linear_act_args_t;
+
+int vf_linear_act_fwd(const vf_linear_act_args_t* args, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Residual add + LayerNorm of the DeBERTa-v2 encoder: out = LayerNorm(x + residual) with
  * weight and bias over the last dimension.  Replaces the two torch kernels of
  * models/deberta_v2/deberta_v2_encoder.py:507 and :566 (`self.LayerNorm(hidden_states +

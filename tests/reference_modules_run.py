@@ -183,6 +183,34 @@ def run(device, lens, seed=0, oracle_kernels=None):
             del v2.DisentangledSelfAttentionV2._vf_reference_flash_forward
     results["deberta_v2"] = res
 
+    if packed:
+        # DebertaV2Intermediate (dense + exact GELU) with the GEMM-epilogue GELU installed on the
+        # reference's class, against its own bf16 forward and an fp32 twin.
+        from kernels import linear_act
+        make_i = lambda: v2.DebertaV2Intermediate(cfg, prefix="check.intermediate").eval()  # noqa: E731
+        inter = make_i()
+        _init(inter, gen, 0.03)
+        inter = inter.to(dev, bf)
+        x_i = torch.randn(B, L, E, generator=gen).to(dev)
+        twin = make_i()
+        with torch.no_grad():
+            src = dict(inter.named_parameters())
+            for name, p in twin.named_parameters():
+                p.copy_(src[name].float().cpu())
+            twin = twin.to(dev, torch.float32)
+            ref_i = twin(x_i)
+            theirs = inter(x_i.to(bf))
+            linear_act.install_fused_intermediate(v2.DebertaV2Intermediate)
+            try:
+                ours = inter(x_i.to(bf))
+            finally:
+                v2.DebertaV2Intermediate.forward = v2.DebertaV2Intermediate._vf_reference_forward
+                del v2.DebertaV2Intermediate._vf_reference_forward
+        results["deberta_v2_intermediate"] = {"fused": _compare(ours, ref_i, lens),
+                                              "torch_bf16": _compare(theirs, ref_i, lens),
+                                              "kernel_module": linear_act.linear_gelu.__module__,
+                                              "kernel_file": linear_act.__file__}
+
     # --- DeBERTa v1 (linear positions, separate position projections)
     import models.deberta.deberta_encoder as v1
     from transformers import DebertaConfig

@@ -20,7 +20,7 @@ def _run(args, env_extra=None, timeout=240):
     return [l for l in res.stdout.splitlines() if l.startswith("{")]
 
 
-@pytest.mark.parametrize("workload", ["mt5_c2", "deberta_add_ln"])
+@pytest.mark.parametrize("workload", ["mt5_c2", "deberta_add_ln", "deberta_ffn_gemm"])
 def test_reference_arm_line(workload):
     lines = _run(["--impl", "reference", "--workload", workload, "--steps", "3", "--warmup", "3"])
     assert len(lines) == 1

@@ -60,3 +60,15 @@ def test_reference_layer_flash_path_matches_its_pytorch_path(results, layer):
         assert ours["min_row_cos"] >= 0.9995, (mode, r)
         assert ours["max_abs"] <= 1.5 * theirs["max_abs"] + 1e-3, (mode, r)
         assert 1.0 - ours["min_row_cos"] <= 1.5 * (1.0 - theirs["min_row_cos"]) + 1e-5, (mode, r)
+
+
+def test_reference_deberta_intermediate_with_fused_gelu(results):
+    """DebertaV2Intermediate (models/deberta_v2/deberta_v2_encoder.py:535-550) with the dense
+    layer and exact GELU as one GEMM (kernels.linear_act installed on the class), against its
+    fp32 twin: within max-abs 2e-2 / cosine 0.9995 and no further than 1.5x its own bf16 path."""
+    r = results["deberta_v2_intermediate"]
+    assert r["kernel_module"] == "kernels.linear_act", r
+    assert Path(r["kernel_file"]).resolve().is_relative_to(ROOT / "vllm-factory_b200"), r
+    ours, theirs = r["fused"], r["torch_bf16"]
+    assert ours["max_abs"] <= 2e-2 and ours["min_row_cos"] >= 0.9995, r
+    assert ours["max_abs"] <= 1.5 * theirs["max_abs"] + 1e-3, r

@@ -140,6 +140,14 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void*
                :: "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
                : "memory");
 }
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               :: "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(c0), "r"(c1) : "memory");
+}
+// The thread's committed bulk stores other than the newest N have finished reading shared memory.
+template <int N> __device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" :: "n"(N) : "memory");
+}
 // Untiled bulk copy shared -> global (async proxy), bulk-group completion; addresses
 // 16-byte aligned, size a multiple of 16.
 __device__ __forceinline__ void bulk_copy_s2g(void* dst, const void* src, uint32_t bytes) {
@@ -479,6 +487,18 @@ __device__ __forceinline__ void add_f16x2_f32(float& acc_lo, float& acc_hi, uint
 // Named barrier over `nthreads` threads (a multiple of 32).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+// Named barrier over `nthreads` threads that also returns whether `pred` held on any of them
+// (a decision every participating thread takes alike).
+__device__ __forceinline__ bool named_bar_any(uint32_t id, uint32_t nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %3, 0;\n\t"
+      "bar.red.or.pred p, %1, %2, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(r) : "r"(id), "r"(nthreads), "r"(pred ? 1u : 0u) : "memory");
+  return r != 0;
 }
 // Arrives on a named barrier without waiting (the producer side of a hand-over).
 __device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t nthreads) {

@@ -541,6 +541,78 @@ at::Tensor add_layer_norm_cpu(const at::Tensor&, const at::Tensor&, const at::Te
   TORCH_CHECK(false, "vf_b200: x and residual must be CUDA tensors (no CPU implementation)");
 }
 
+// ---------------------------------------------------------------- linear + activation
+// act(x W^T + bias), or act(x W^T) * mul, over the last dimension of x (any leading shape),
+// the activation in the GEMM's epilogue (vf_linear_act_fwd).
+at::Tensor linear_act(const at::Tensor& x_in, const at::Tensor& w_in, const std::optional<at::Tensor>& bias_opt,
+                      const std::optional<at::Tensor>& mul_opt, int64_t act) {
+  require_cuda(x_in, "x");
+  require_cuda(w_in, "weight");
+  TORCH_CHECK(w_in.dim() == 2, "vf_b200: weight must be [out_features, in_features]");
+  TORCH_CHECK(x_in.dim() >= 1 && x_in.size(-1) == w_in.size(1), "vf_b200: x's last dimension must be in_features = ",
+              w_in.size(1));
+  TORCH_CHECK(x_in.scalar_type() == w_in.scalar_type(), "vf_b200: x and weight must share a dtype");
+  c10::cuda::CUDAGuard guard(x_in.device());
+  const int64_t K = w_in.size(1), N = w_in.size(0);
+  const int64_t rows = K == 0 ? 0 : x_in.numel() / K;
+  std::vector<int64_t> out_shape(x_in.sizes().begin(), x_in.sizes().end());
+  out_shape.back() = N;
+  at::Tensor out = at::empty(out_shape, x_in.options());
+  if (rows == 0) return out;
+  const int64_t es = x_in.element_size();
+  auto rows_ok = [&](const at::Tensor& t) {
+    return t.stride(-1) == 1 && (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) == 0 &&
+           (t.size(0) <= 1 || ((t.stride(0) * es) % 16 == 0 && t.stride(0) >= t.size(1)));
+  };
+  at::Tensor x = as_rows(x_in, rows, K);
+  if (!rows_ok(x)) x = x.contiguous();
+  at::Tensor w = rows_ok(w_in) ? w_in : w_in.contiguous();
+  const bool gated = mul_opt.has_value() && mul_opt->defined();
+  at::Tensor bias, mul;
+  if (gated) {
+    // out = act(x W^T) * mul: the gated form takes no bias.
+    require_cuda(*mul_opt, "mul");
+    TORCH_CHECK(!(bias_opt.has_value() && bias_opt->defined()), "vf_b200: the gated form (mul) takes no bias");
+    TORCH_CHECK(mul_opt->scalar_type() == x.scalar_type(), "vf_b200: mul must have x's dtype");
+    TORCH_CHECK(mul_opt->numel() == rows * N && mul_opt->size(-1) == N, "vf_b200: mul must be [..., out_features] like the result");
+    mul = as_rows(*mul_opt, rows, N);
+    if (!rows_ok(mul)) mul = mul.contiguous();
+  } else if (bias_opt.has_value() && bias_opt->defined()) {
+    require_cuda(*bias_opt, "bias");
+    TORCH_CHECK(bias_opt->dim() == 1 && bias_opt->size(0) == N, "vf_b200: bias must be [out_features]");
+    bias = bias_opt->to(x.scalar_type()).contiguous();
+  } else {
+    bias = at::zeros({N}, x.options());
+  }
+  vf_linear_act_args_t a{};
+  a.dtype = dtype_code(x);
+  a.x = x.data_ptr();
+  a.weight = w.data_ptr();
+  a.bias = gated ? nullptr : bias.data_ptr();
+  a.mul = gated ? mul.data_ptr() : nullptr;
+  a.mul_row_stride = gated ? (rows > 1 ? mul.stride(0) : N) : 0;
+  a.out = out.data_ptr();
+  a.rows = rows;
+  a.K = K;
+  a.N = N;
+  a.x_row_stride = rows > 1 ? x.stride(0) : K;
+  a.weight_row_stride = N > 1 ? w.stride(0) : K;
+  a.out_row_stride = N;
+  a.act = static_cast<int32_t>(act);
+  check_rc(vf_linear_act_fwd(&a, at::cuda::getCurrentCUDAStream().stream()));
+  return out;
+}
+at::Tensor linear_act_meta(const at::Tensor& x, const at::Tensor& w, const std::optional<at::Tensor>&,
+                           const std::optional<at::Tensor>&, int64_t) {
+  std::vector<int64_t> out_shape(x.sizes().begin(), x.sizes().end());
+  out_shape.back() = w.size(0);
+  return at::empty(out_shape, x.options());
+}
+at::Tensor linear_act_cpu(const at::Tensor&, const at::Tensor&, const std::optional<at::Tensor>&,
+                          const std::optional<at::Tensor>&, int64_t) {
+  TORCH_CHECK(false, "vf_b200: x and weight must be CUDA tensors (no CPU implementation)");
+}
+
 // ---------------------------------------------------------------- GLiNER span scores
 // Rows of a 2-D 16-bit operand as the kernel reads them: unit column stride, 16-byte aligned
 // base and row stride (else a contiguous copy).
@@ -701,6 +773,7 @@ TORCH_LIBRARY(vf_b200, m) {
   m.def("deberta_attention_fused_varlen(Tensor q, Tensor k, Tensor v, Tensor cu_seqlens, int max_seqlen, "
         "Tensor? rel_key, Tensor? rel_query, bool causal, float? sm_scale, int position_buckets, "
         "int max_relative_distance, bool use_log_bucket) -> Tensor");
+  m.def("linear_act(Tensor x, Tensor weight, Tensor? bias, Tensor? mul, int act) -> Tensor");
   m.def("span_scores(Tensor start_proj, Tensor end_proj, Tensor span_idx, Tensor classes, Tensor? class_bias, "
         "int[] word_offsets, int[] span_offsets, int[] class_offsets, ScalarType out_dtype) -> Tensor");
 }
@@ -715,6 +788,7 @@ TORCH_LIBRARY_IMPL(vf_b200, CUDA, m) {
   m.impl("gated_act", &gated_act);
   m.impl("add_layer_norm", &add_layer_norm);
   m.impl("span_scores", &span_scores);
+  m.impl("linear_act", &linear_act);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
@@ -727,6 +801,7 @@ TORCH_LIBRARY_IMPL(vf_b200, CPU, m) {
   m.impl("gated_act", &gated_act_cpu);
   m.impl("add_layer_norm", &add_layer_norm_cpu);
   m.impl("span_scores", &span_scores_cpu);
+  m.impl("linear_act", &linear_act_cpu);
 }
 
 TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
@@ -739,4 +814,5 @@ TORCH_LIBRARY_IMPL(vf_b200, Meta, m) {
   m.impl("gated_act", &gated_act_meta);
   m.impl("add_layer_norm", &add_layer_norm_meta);
   m.impl("span_scores", &span_scores_meta);
+  m.impl("linear_act", &linear_act_meta);
 }

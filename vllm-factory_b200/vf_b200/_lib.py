@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "vf_gated_act_fwd",
     "vf_add_layer_norm_fwd",
     "vf_span_scores_fwd",
+    "vf_linear_act_fwd",
     "vf_t5_relative_bucket",
     "vf_deberta_log_bucket",
     "vf_last_error",
@@ -110,6 +111,25 @@ class AddLayerNormArgs(ctypes.Structure):
         ("residual_row_stride", ctypes.c_int64),
         ("out_row_stride", ctypes.c_int64),
         ("eps", ctypes.c_float),
+    ]
+
+
+class LinearActArgs(ctypes.Structure):
+    _fields_ = [
+        ("dtype", ctypes.c_int),
+        ("x", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("mul", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("rows", ctypes.c_int64),
+        ("K", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+        ("x_row_stride", ctypes.c_int64),
+        ("weight_row_stride", ctypes.c_int64),
+        ("mul_row_stride", ctypes.c_int64),
+        ("out_row_stride", ctypes.c_int64),
+        ("act", ctypes.c_int32),
     ]
 
 
@@ -227,6 +247,8 @@ def load() -> ctypes.CDLL:
         lib.vf_add_layer_norm_fwd.restype = ctypes.c_int
         lib.vf_span_scores_fwd.argtypes = [ctypes.POINTER(SpanScoresArgs), ctypes.c_void_p]
         lib.vf_span_scores_fwd.restype = ctypes.c_int
+        lib.vf_linear_act_fwd.argtypes = [ctypes.POINTER(LinearActArgs), ctypes.c_void_p]
+        lib.vf_linear_act_fwd.restype = ctypes.c_int
         lib.vf_t5_relative_bucket.argtypes = [ctypes.c_int32] * 5 + [ctypes.POINTER(ctypes.c_int32)]
         lib.vf_t5_relative_bucket.restype = ctypes.c_int
         lib.vf_deberta_log_bucket.argtypes = [ctypes.c_int32] * 4 + [ctypes.POINTER(ctypes.c_int32)]

@@ -18,7 +18,7 @@ INCLUDE = PKG_DIR.parent.parent / "include"
 LIB_PATH = PKG_DIR / "libvf_b200.so"
 TORCH_LIB_PATH = PKG_DIR / "libvf_b200_torch.so"
 SOURCES = [CSRC / "vf_attention.cu", CSRC / "vf_deberta_fused.cu", CSRC / "vf_ffn.cu", CSRC / "vf_layernorm.cu",
-           CSRC / "vf_span.cu"]
+           CSRC / "vf_span.cu", CSRC / "vf_gemm.cu"]
 DEPS = SOURCES + [CSRC / "vf_ptx.cuh", CSRC / "vf_internal.h", INCLUDE / "vf_b200.h"]
 TORCH_SOURCES = [CSRC / "vf_torch_ops.cpp"]
 TORCH_DEPS = TORCH_SOURCES + [INCLUDE / "vf_b200.h"]

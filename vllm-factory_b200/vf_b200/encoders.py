@@ -25,6 +25,7 @@ views.
 from __future__ import annotations
 
 import math
+from typing import Optional
 from dataclasses import dataclass
 
 import torch
@@ -93,7 +94,8 @@ class DebertaV3Encoder:
     any function of the same signature, e.g. a CPU oracle)."""
 
     def __init__(self, cfg: DebertaConfig = DebertaConfig(), device="cuda", dtype=torch.bfloat16, seed: int = 0,
-                 attention_fn=None, add_norm=None, act_fn=None, fused_positions: bool = True):
+                 attention_fn=None, add_norm=None, act_fn=None, fused_positions: bool = True,
+                 fused_ffn: Optional[bool] = None):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         g = torch.Generator(device=self.device).manual_seed(seed)
         E, F_, S2 = cfg.hidden, cfg.ffn, 2 * cfg.position_buckets
@@ -122,6 +124,12 @@ class DebertaV3Encoder:
         # package's activation-only kernel, measured the same C3 tokens/s in its place
         self.act_fn = F.gelu if act_fn is None else act_fn
         self.fused_positions = fused_positions
+        # The feed-forward's dense layer + exact GELU as one GEMM with the activation in its
+        # epilogue (kernels.linear_act), unless another activation was given.
+        self.fused_ffn = (act_fn is None) if fused_ffn is None else fused_ffn
+        if self.fused_ffn:
+            from kernels.linear_act import linear_gelu
+            self.linear_gelu = linear_gelu
 
     @torch.no_grad()
     def forward(self, ids: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
@@ -148,7 +156,10 @@ class DebertaV3Encoder:
                                         cfg.position_buckets, cfg.max_relative_positions, True)
             a = torch.addmm(L["bo"], ctx.reshape(T, E).to(h.dtype), L["wo"].t())
             h = self.add_norm(a, h, *L["ln1"], cfg.eps)
-            f = self.act_fn(torch.addmm(L["b1"], h, L["w1"].t()))
+            if self.fused_ffn:
+                f = self.linear_gelu(h, L["w1"], L["b1"])
+            else:
+                f = self.act_fn(torch.addmm(L["b1"], h, L["w1"].t()))
             h = self.add_norm(torch.addmm(L["b2"], f, L["w2"].t()), h, *L["ln2"], cfg.eps)
         return h
 
@@ -158,8 +169,8 @@ class DebertaV3Encoder:
 
     def own_launches_per_layer(self) -> int:
         """This package's kernel launches per layer: the attention (with the fused mode's
-        set-up kernel) and two add + LayerNorm."""
-        return 4 if self.fused_positions else 3
+        set-up kernel), two add + LayerNorm and the fused dense + GELU."""
+        return (4 if self.fused_positions else 3) + (1 if self.fused_ffn else 0)
 
 
 class MT5Encoder:
@@ -168,7 +179,7 @@ class MT5Encoder:
     same signatures)."""
 
     def __init__(self, cfg: MT5Config = MT5Config(), device="cuda", dtype=torch.bfloat16, seed: int = 0,
-                 attention_fn=None, gated_act=None):
+                 attention_fn=None, gated_act=None, fused_ffn: Optional[bool] = None):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         g = torch.Generator(device=self.device).manual_seed(seed)
         E, F_ = cfg.hidden, cfg.ffn
@@ -185,9 +196,15 @@ class MT5Encoder:
         if attention_fn is None:
             from kernels.flash_attention_rpb import flash_attention_rpb_varlen as attention_fn
         self.attention_fn = attention_fn
+        # The gated-GELU in the gate projection's GEMM epilogue (kernels.linear_act), unless
+        # another activation function was given: up = x wi_1^T, then gelu_tanh(x wi_0^T) * up.
+        self.fused_ffn = (gated_act is None) if fused_ffn is None else fused_ffn
         if gated_act is None:
             from kernels.ff_fused import fused_gelu_mul_dropout as gated_act
         self.gated_act = gated_act
+        if self.fused_ffn:
+            from kernels.linear_act import gated_gelu_tanh
+            self.gated_gelu_tanh = gated_gelu_tanh
 
     @torch.no_grad()
     def forward(self, ids: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int) -> torch.Tensor:
@@ -201,8 +218,12 @@ class MT5Encoder:
                                     cfg.num_buckets, cfg.max_distance, False, 1.0)
             h = h + ctx.reshape(T, E).to(h.dtype) @ L["wo"].t()
             x = _rms_norm(h, L["ln2"], cfg.eps)
-            gu = x @ L["wi"].t()
-            f = self.gated_act(gu[:, :F_], gu[:, F_:], "gelu_new")     # gated-GELU, halves read in place
+            if self.fused_ffn:
+                up = x @ L["wi"][F_:].t()
+                f = self.gated_gelu_tanh(x, L["wi"][:F_], up)
+            else:
+                gu = x @ L["wi"].t()
+                f = self.gated_act(gu[:, :F_], gu[:, F_:], "gelu_new")     # gated-GELU, halves read in place
             h = h + f @ L["wo_ff"].t()
         return _rms_norm(h, self.final_ln, cfg.eps)
 
