@@ -58,9 +58,12 @@ typedef struct {
  *
  * q, k, v, out: (B, H, M|N, 64), dtype 16-bit (f16/bf16), innermost stride 1.
  * rpb_table: (num_table_rows, H) 2-D with the given element strides, or NULL (no bias).
- * padding_mask: additive, broadcastable (B|1, H|1, 1, N); data NULL = none.
- * Rows of a batch whose padding mask is <= -1e4 on every key of a 128-key tile make
- * that tile contribute exactly zero, so such tiles at either end are skipped.
+ * padding_mask: additive, broadcastable (B|1, H|1, 1|M, N), bf16 / f16 / f32 (mask_dtype);
+ * data NULL = none.  A mask that broadcasts over query rows (1) is staged per key tile:
+ * rows of a batch whose mask is <= -1e4 on every key of a 128-key tile make that tile
+ * contribute exactly zero, so such tiles at either end are skipped.  A mask that varies
+ * over query rows (M; the reference reads it with stride_mask_m, :182-185) is added per
+ * score by a second kernel instance that visits every key tile.
  * ------------------------------------------------------------------------------------ */
 typedef struct {
   vf_dtype_t dtype;

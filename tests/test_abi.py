@@ -91,6 +91,18 @@ def test_rpb_validation_rejects_before_launch(kwargs, code):
     assert lib.vf_last_error().decode()
 
 
+@pytest.mark.parametrize("mshape,msg", [((2, 1, 7, 256), "query dim"), ((2, 1, 256, 255), "last dim"),
+                                         ((3, 1, 256, 256), "batch dim"), ((2, 3, 1, 256), "head dim")])
+def test_rpb_mask_shapes_rejected_before_launch(mshape, msg):
+    """A padding mask broadcasts over (B|1, H|1, 1|M, N); other shapes fail before any launch."""
+    lib = _lib.load()
+    a = _rpb_args()
+    a.padding_mask = _fake_t4(mshape, 0x80000)
+    a.mask_dtype = _lib.VF_DTYPE_BF16
+    assert lib.vf_rpb_attention_fwd(ctypes.byref(a), None) == _lib.VF_EINVAL
+    assert msg in lib.vf_last_error().decode()
+
+
 def test_rpb_null_and_shape_mismatch():
     lib = _lib.load()
     assert lib.vf_rpb_attention_fwd(None, None) == _lib.VF_EINVAL

@@ -68,3 +68,34 @@ torch.cuda.synchronize()
                          text=True, timeout=300)
     assert res.returncode == 0, f"exit {res.returncode}\n{res.stdout[-2000:]}\n{res.stderr[-4000:]}"
     assert "RAISED" in res.stdout, res.stdout
+
+
+@pytest.mark.gpu
+def test_device_error_check_mode_raises_on_bad_packed_offsets():
+    """With VF_B200_CHECK_DEVICE_ERRORS=1 every op synchronises after its launch and raises
+    when a kernel set the device error word: here decreasing packed offsets (bit 2; the kernel
+    clamps the rows it uses into the views and returns).  Without the variable the same call
+    returns and only vf_device_error reports it."""
+    import os
+    call = """
+q = torch.randn(200, 2, 64, dtype=bf, device=dev)
+t = torch.randn(32, 2, dtype=bf, device=dev)
+bad = torch.tensor([100, 40, 160], dtype=torch.int32, device=dev)
+torch.ops.vf_b200.rpb_attention_varlen(q, q, q, bad, 100, t, 32, 128, False, 1.0)
+"""
+    code = PRELUDE + textwrap.dedent(f"""
+import vf_b200
+vf_b200.device_error(clear=True)
+try:
+{textwrap.indent(textwrap.dedent(call).strip(), '    ')}
+    torch.cuda.synchronize()
+    print("RETURNED", vf_b200.device_error(clear=True) & 4)
+except RuntimeError as e:
+    print("RAISED", str(e).splitlines()[0])
+""")
+    for flag, want in (("1", "RAISED vf_b200: a kernel reported device error word"), ("0", "RETURNED 4")):
+        env = dict(os.environ, VF_B200_CHECK_DEVICE_ERRORS=flag)
+        res = subprocess.run([sys.executable, "-X", "faulthandler", "-c", code], cwd=ROOT, capture_output=True,
+                             text=True, timeout=300, env=env)
+        assert res.returncode == 0, f"exit {res.returncode}\n{res.stdout[-2000:]}\n{res.stderr[-4000:]}"
+        assert want in res.stdout, res.stdout

@@ -176,3 +176,59 @@ def test_rpb_many_short_sequences_natural_order():
     lens = [1 + (37 * b) % L for b in range(B)]
     q, k, v, t, m = make_inputs(B, 1, L, L, torch.bfloat16, lens=lens, seed=31)
     check(q, k, v, t, m, what="1100 sequences")
+
+
+def _query_mask(B, H, M, N, dtype, seed, heads=1):
+    """An additive mask that varies over query rows: a random pattern of blocked (finfo.min)
+    keys per row, a band of small finite offsets, and one row whose every key is blocked."""
+    g = torch.Generator().manual_seed(seed)
+    blocked = torch.rand(B, heads, M, N, generator=g) < 0.3
+    mask = (torch.randn(B, heads, M, N, generator=g) * 0.5).float()
+    mask[blocked] = float(torch.finfo(dtype).min)
+    mask[:, :, M // 3, :] = float(torch.finfo(dtype).min)
+    return mask.to(dtype)
+
+
+@pytest.mark.parametrize("M,N,heads,dtype", [(300, 300, 1, torch.bfloat16), (129, 513, 2, torch.bfloat16),
+                                             (256, 256, 2, torch.float16), (700, 700, 1, torch.bfloat16)])
+def test_rpb_query_varying_mask(M, N, heads, dtype):
+    """A padding mask that varies over query rows ([B|1, H|1, M, N], reference
+    kernels/flash_attention_rpb.py:182-185 reads it with stride_mask_m) runs in its own kernel
+    instance and matches the oracle, the blocked-everywhere row included.  Gate: row cosine
+    0.9999 and max-abs within the 16-bit rounding bound (see _check_qmask)."""
+    q, k, v, t, _ = make_inputs(2, 2, M, N, dtype, seed=M + N)
+    mask = _query_mask(2, 2, M, N, dtype, seed=M, heads=heads)
+    _check_qmask(q, k, v, t, mask, what=f"qmask M={M} N={N} heads={heads}")
+
+
+def _check_qmask(q, k, v, t, mask, is_decoder=False, what=""):
+    op = _import_op()
+    dev = torch.device("cuda")
+    out = op(q.to(dev), k.to(dev), v.to(dev), t.to(dev), 32, 128, is_decoder, mask.to(dev), 0.0, 1.0)
+    torch.cuda.synchronize()
+    ref = oracle.rpb_attention_ref(q.float(), k.float(), v.float(), t.float(), 32, 128, is_decoder, mask.float(), 1.0)
+    assert out.shape == q.shape and torch.isfinite(out.float()).all(), what
+    # Max-abs bound: the probabilities are rounded to the 16-bit dtype before P V, unnormalised
+    # (flash-attention style: up to one unit roundoff u on the dominant term, |v| <= max|v|),
+    # and the output is rounded once more (u |out| <= u max|v|); 2e-2 floor, 1.25x margin.
+    # With 30 % of keys blocked, the unscaled q.k of unit-variance inputs makes rows peaked,
+    # so these roundings reach ~3e-2 on a 2 x 2 x 700 x 64 output.
+    u = 2.0 ** -8 if q.dtype == torch.bfloat16 else 2.0 ** -11
+    gate = max(2e-2, 1.25 * 2 * u * v.float().abs().max().item())
+    assert_close(out, ref, None, max_abs=gate, what=what)
+
+
+def test_rpb_query_varying_mask_strided_and_broadcast():
+    """Non-contiguous (a column slice: the per-element load path) and batch-broadcast query
+    masks, and the decoder's causal mask on top of a query mask."""
+    M = N = 260
+    q, k, v, t, _ = make_inputs(2, 2, M, N, torch.bfloat16, seed=11)
+    wide = _query_mask(2, 1, M, N + 6, torch.bfloat16, seed=12)[..., 3:N + 3]
+    assert not wide.is_contiguous()
+    _check_qmask(q, k, v, t, wide, what="qmask strided")
+    bmask = _query_mask(1, 1, M, N, torch.bfloat16, seed=13)
+    _check_qmask(q, k, v, t, bmask, what="qmask batch-broadcast")
+    _check_qmask(q, k, v, t, bmask, is_decoder=True, what="qmask decoder")
+    fmask = _query_mask(2, 2, M, N, torch.float32, seed=14)
+    _check_qmask(q, k, v, t, fmask, what="qmask fp32 mask")
+

@@ -108,6 +108,11 @@ struct __align__(64) KParams {
   const void* mask;
   long long mk_sb, mk_sh, mk_sn;
   int mask_dtype;
+  // T5 mask that varies over query rows (additive, [B|1, H|1, M, N]; the kernel instance
+  // with kQMask reads it per score; `mask` is then null and mask_dtype gives its type)
+  const void* qmask;
+  long long qm_sb, qm_sh, qm_sm, qm_sn;
+  int qmask_vec;         // 16-bit, unit column stride, 16-byte aligned rows: 16-byte loads
   // DeBERTa positions
   const void* pos_key;
   long long pk_sb, pk_sh, pk_sm, pk_sk;
@@ -380,7 +385,7 @@ __device__ __forceinline__ bool unit_coords(const KParams& p, const uint16_t* or
   return true;
 }
 
-template <int kVariant, typename T>
+template <int kVariant, typename T, bool kQMask = false>
 __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_constant__ KParams p) {
   using S = Smem<kVariant>;
   constexpr int KV = S::kKV, QB = S::kQBuf;
@@ -819,7 +824,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
           const float2* kb2 = reinterpret_cast<const float2*>(kbias + st * kBN);
           const int klen = vu->klen;
           const bool edge = (k0 + kBN > klen) || (p.causal && r_hi > 0);
-          if (saturated && !kadd && !edge && scale_log2 > 0.f) {
+          if (!kQMask && saturated && !kadd && !edge && scale_log2 > 0.f) {
             // Constant bias: keep raw S; max(s * sc + cb) = max(s) * sc + cb, and the
             // exponent pass computes s * sc + (cb - m) in one FMA.
             const_bias = true;
@@ -837,6 +842,37 @@ __global__ void __launch_bounds__(kThreads, 1) attn_fwd_kernel(const __grid_cons
             } else {
 #pragma unroll
               for (int j = 0; j < kBN / 2; ++j) x2[j] = __ffma2_rn(x2[j], sc2, make_float2(rb[2 * j], rb[2 * j + 1]));
+            }
+          }
+          if constexpr (kQMask) {
+            // The caller's mask row m (rows past M read row M - 1; their output is not
+            // stored), clamped like the key mask, in log2 units.
+            const long long rowbase = vu->b * p.qm_sb + vu->h * p.qm_sh + (long long)min(m, p.M - 1) * p.qm_sm;
+            if (p.qmask_vec && k0 + kBN <= p.N) {
+              const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.qmask) + rowbase + k0);
+              const bool bf = p.mask_dtype == VF_DTYPE_BF16;
+#pragma unroll
+              for (int q8 = 0; q8 < kBN / 8; ++q8) {
+                const uint4 w = __ldg(src + q8);
+                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const uint16_t lo = static_cast<uint16_t>(ws[e] & 0xffffu), hi = static_cast<uint16_t>(ws[e] >> 16);
+                  const float flo = bf ? __uint_as_float(static_cast<uint32_t>(lo) << 16) : __half2float(__ushort_as_half(lo));
+                  const float fhi = bf ? __uint_as_float(static_cast<uint32_t>(hi) << 16) : __half2float(__ushort_as_half(hi));
+                  x2[4 * q8 + e] = __ffma2_rn(make_float2(fmaxf(flo, kMaskFloor), fmaxf(fhi, kMaskFloor)),
+                                              make_float2(kLog2e, kLog2e), x2[4 * q8 + e]);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < kBN / 2; ++j) {   // fully unrolled: x2 stays in registers
+                const int n = k0 + 2 * j;
+                const float a0 = n < p.N ? load_any(p.qmask, rowbase + n * p.qm_sn, p.mask_dtype) : 0.f;
+                const float a1 = n + 1 < p.N ? load_any(p.qmask, rowbase + (n + 1) * p.qm_sn, p.mask_dtype) : 0.f;
+                x2[j] = __ffma2_rn(make_float2(fmaxf(a0, kMaskFloor), fmaxf(a1, kMaskFloor)),
+                                   make_float2(kLog2e, kLog2e), x2[j]);
+              }
             }
           }
           if (edge) {
@@ -1268,9 +1304,9 @@ int check_qkv(const vf_tensor4d_t& q, const vf_tensor4d_t& k, const vf_tensor4d_
   return VF_OK;
 }
 
-template <int kVariant, typename T>
+template <int kVariant, typename T, bool kQMask = false>
 int launch(vf::KParams* kp, cudaStream_t stream) {
-  auto kern = vf::attn_fwd_kernel<kVariant, T>;
+  auto kern = vf::attn_fwd_kernel<kVariant, T, kQMask>;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::once_flag flags[64];
@@ -1476,7 +1512,10 @@ int vf_device_error(int32_t clear) {
   unsigned int span_word = 0;
   e = vf::span_take_error_word(clear != 0, &span_word);
   if (e != cudaSuccess) return fail(VF_ECUDA, std::string("reading the device error word: ") + cudaGetErrorString(e));
-  return static_cast<int>((word | fused_word | span_word) & 0x7fffffff);
+  unsigned int gemm_word = 0;
+  e = vf::gemm_take_error_word(clear != 0, &gemm_word);
+  if (e != cudaSuccess) return fail(VF_ECUDA, std::string("reading the device error word: ") + cudaGetErrorString(e));
+  return static_cast<int>((word | fused_word | span_word | gemm_word) & 0x7fffffff);
 }
 
 int vf_selftest_wait_timeout(int64_t limit_cycles, void* stream) {
@@ -1510,25 +1549,46 @@ int vf_deberta_log_bucket(int32_t bucket_size, int32_t max_position, int32_t rmi
 
 int vf_rpb_attention_fwd(const vf_rpb_attention_args_t* a, void* stream) {
   if (a == nullptr) return fail(VF_EINVAL, "null args");
+  // The mask's shape is checked first (before any driver call).
+  const vf_tensor4d_t& mk = a->padding_mask;
+  const bool query_mask = mk.data != nullptr && mk.size[2] != 1 && mk.stride[2] != 0;
+  if (mk.data != nullptr) {
+    if (query_mask && mk.size[2] != a->q.size[2])
+      return fail(VF_EINVAL, "rpb attention: padding_mask query dim must be 1 or the query length");
+    if (mk.size[3] != a->k.size[2]) return fail(VF_EINVAL, "rpb attention: padding_mask last dim must equal key length");
+    if (mk.size[0] != 1 && mk.size[0] != a->q.size[0]) return fail(VF_EINVAL, "rpb attention: padding_mask batch dim");
+    if (mk.size[1] != 1 && mk.size[1] != a->q.size[1]) return fail(VF_EINVAL, "rpb attention: padding_mask head dim");
+  }
   static thread_local vf::KParams kp;
   int rc = rpb_prepare(a, &kp);
   if (rc) return rc;
-  const int H = kp.H, N = kp.N;
-  if (a->padding_mask.data != nullptr) {
-    const vf_tensor4d_t& mk = a->padding_mask;
-    if (mk.size[2] != 1 && mk.stride[2] != 0)
-      return fail(VF_EUNSUPPORTED, "rpb attention: padding_mask must broadcast over query rows ([B|1, H|1, 1, N])");
-    if (mk.size[3] != N) return fail(VF_EINVAL, "rpb attention: padding_mask last dim must equal key length");
-    if (mk.size[0] != 1 && mk.size[0] != a->q.size[0]) return fail(VF_EINVAL, "rpb attention: padding_mask batch dim");
-    if (mk.size[1] != 1 && mk.size[1] != H) return fail(VF_EINVAL, "rpb attention: padding_mask head dim");
-    kp.mask = mk.data;
-    kp.mk_sb = mk.size[0] > 1 ? mk.stride[0] : 0;
-    kp.mk_sh = mk.size[1] > 1 ? mk.stride[1] : 0;
-    kp.mk_sn = mk.size[3] > 1 ? mk.stride[3] : 0;
+  kp.qmask = nullptr;
+  if (mk.data != nullptr) {
     kp.mask_dtype = a->mask_dtype;
+    const long long sb = mk.size[0] > 1 ? mk.stride[0] : 0, sh = mk.size[1] > 1 ? mk.stride[1] : 0;
+    const long long sn = mk.size[3] > 1 ? mk.stride[3] : 0;
+    if (query_mask) {
+      // A mask that varies over query rows: a kernel instance that adds mask[b, h, m, n] to
+      // each score (every key tile of a row visited); the per-key mask path stays off.
+      kp.mask = nullptr;
+      kp.qmask = mk.data;
+      kp.qm_sb = sb;
+      kp.qm_sh = sh;
+      kp.qm_sm = mk.stride[2];
+      kp.qm_sn = sn;
+      kp.qmask_vec = a->mask_dtype != VF_DTYPE_F32 && sn == 1 && sb % 8 == 0 && sh % 8 == 0 &&
+                     kp.qm_sm % 8 == 0 && (reinterpret_cast<uintptr_t>(mk.data) & 15) == 0;
+    } else {
+      kp.mask = mk.data;
+      kp.mk_sb = sb;
+      kp.mk_sh = sh;
+      kp.mk_sn = sn;
+    }
   }
   if ((rc = finish_rpb_table(a, std::max(kp.M, kp.N), &kp))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (query_mask)
+    return a->dtype == VF_DTYPE_BF16 ? launch<vf::kT5, __nv_bfloat16, true>(&kp, s) : launch<vf::kT5, __half, true>(&kp, s);
   return a->dtype == VF_DTYPE_BF16 ? launch<vf::kT5, __nv_bfloat16>(&kp, s) : launch<vf::kT5, __half>(&kp, s);
 }
 

@@ -305,6 +305,10 @@ __global__ void __launch_bounds__(kThreads, 1) linear_act_kernel(const __grid_co
 }
 
 }  // namespace gemm
+
+// Error word of this file (vf_device_error gathers it).
+cudaError_t gemm_take_error_word(bool clear, unsigned int* word) { return take_error_word(clear, word); }
+
 }  // namespace vf
 
 // =====================================================================================

@@ -39,4 +39,7 @@ cudaError_t fused_take_error_word(bool clear, unsigned int* word);
 // The same for the span-score kernel file (vf_span.cu).
 cudaError_t span_take_error_word(bool clear, unsigned int* word);
 
+// The same for the feed-forward GEMM file (vf_gemm.cu).
+cudaError_t gemm_take_error_word(bool clear, unsigned int* word);
+
 }  // namespace vf

@@ -19,9 +19,12 @@
 #include <algorithm>
 #include <climits>
 #include <cmath>
+#include <cstdlib>
 #include <optional>
 #include <string>
 #include <vector>
+
+#include <cstdlib>
 
 #include "vf_b200.h"
 
@@ -67,8 +70,25 @@ void require_cuda(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), "vf_b200: ", name, " must be a CUDA tensor (no CPU implementation)");
 }
 
+// VF_B200_CHECK_DEVICE_ERRORS=1 (read once): after every launch, synchronise and raise if a
+// kernel set the device error word (a bounded wait that ran out, a failed index check, packed
+// offsets that broke the rules).  A debugging aid: it serialises the caller with the device.
+bool device_error_checks() {
+  static const bool on = [] {
+    const char* v = std::getenv("VF_B200_CHECK_DEVICE_ERRORS");
+    return v != nullptr && v[0] != '\0' && v[0] != '0';
+  }();
+  return on;
+}
+
 void check_rc(int rc) {
   TORCH_CHECK(rc == VF_OK, "vf_b200 error ", rc, ": ", vf_last_error());
+  if (device_error_checks()) {
+    const int word = vf_device_error(1);
+    TORCH_CHECK(word >= 0, "vf_b200 error ", word, ": ", vf_last_error());
+    TORCH_CHECK(word == 0, "vf_b200: a kernel reported device error word 0x", std::hex, word,
+                " (bit 0: a bounded wait ran out; bit 1: an index failed its check; bit 2: packed offsets broke the rules)");
+  }
 }
 
 // fp32 operands become fp16 (clamped to its finite range); 16-bit ones pass through.
