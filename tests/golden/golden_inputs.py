@@ -51,6 +51,8 @@ def t5_case(name: str):
     """Inputs for the mT5 attention path (bias table [buckets, heads], additive mask)."""
     if name == "t5_enc":
         B, H, L, nb, md, lens, seed = 2, 2, 192, 32, 128, [192, 77], 21
+    elif name == "t5_qmask":
+        B, H, L, nb, md, lens, seed = 2, 2, 160, 32, 128, [160, 101], 23
     else:
         raise KeyError(name)
     g = torch.Generator().manual_seed(seed)
@@ -62,6 +64,14 @@ def t5_case(name: str):
     m = (torch.arange(L)[None, :] < torch.tensor(lens)[:, None]).to(torch.float32)
     # models/mt5/mt5_encoder.py:571-576: (1 - m) * finfo(dtype).min, [B, 1, 1, L]
     mask = (1.0 - m[:, None, None, :]) * torch.finfo(torch.bfloat16).min
+    if name == "t5_qmask":
+        # A mask that varies over query rows, [B, 1, L, L]: the padding mask plus blocked keys
+        # per row and small finite offsets (the reference adds any broadcastable mask,
+        # models/mt5/mt5_encoder.py:107-108; its kernel reads it with stride_mask_m).
+        blocked = torch.rand(B, 1, L, L, generator=g) < 0.25
+        extra = _bf16(torch.randn(B, 1, L, L, generator=g) * 0.5)
+        extra = extra.masked_fill(blocked, torch.finfo(torch.bfloat16).min)
+        mask = _bf16(torch.maximum(mask.expand(B, 1, L, L) + extra, torch.full((), torch.finfo(torch.bfloat16).min)))
     return dict(q=q, k=k, v=v, table=table, mask=mask, num_buckets=nb, max_distance=md,
                 lens=torch.tensor(lens, dtype=torch.int32))
 

@@ -103,6 +103,19 @@ def main():
     out["t5_enc_out"] = o.float().numpy()
     for key in ("q", "k", "v", "table", "mask"):
         out[f"t5_enc_sha_{key}"] = np.array(gi.sha(c[key]))
+    # The same path with a mask that varies over query rows ([B, 1, L, L]).
+    c = gi.t5_case("t5_qmask")
+    B, H, L, _ = c["q"].shape
+    rpb = T5RelativePositionBias(c["num_buckets"], c["max_distance"], H)
+    with torch.no_grad():
+        rpb.relative_attention_bias.weight.copy_(c["table"])
+        dense = rpb(L, L, torch.device("cpu"), bidirectional=True)
+        bias = _make_contiguous_additive_bias(dense, c["mask"].float(), B, H, L, L, torch.float32,
+                                              torch.device("cpu"))
+        o = torch.nn.functional.scaled_dot_product_attention(c["q"], c["k"], c["v"], attn_mask=bias, scale=1.0)
+    out["t5_qmask_out"] = o.float().numpy()
+    for key in ("q", "k", "v", "table", "mask"):
+        out[f"t5_qmask_sha_{key}"] = np.array(gi.sha(c[key]))
 
     # ---------------- DeBERTa-v2 layer (_pytorch_forward), fp32
     ctx = _bootstrap_vllm_cpu()

@@ -60,6 +60,18 @@ def test_t5_oracle_matches_reference():
     assert_close(out, ref, None, max_abs=2e-5, min_cos=0.999999, what="t5_enc")
 
 
+def test_t5_oracle_matches_reference_with_query_varying_mask():
+    """A [B, 1, L, L] mask (varies over query rows) through the reference's own bias helper
+    and SDPA: the oracle the query-row-mask kernel instance is checked against."""
+    c = gi.t5_case("t5_qmask")
+    for key in ("q", "k", "v", "table", "mask"):
+        assert gi.sha(c[key]) == str(G[f"t5_qmask_sha_{key}"])
+    out = oracle.rpb_attention_ref(c["q"], c["k"], c["v"], c["table"], c["num_buckets"], c["max_distance"],
+                                   False, c["mask"], 1.0, dtype=torch.float32)
+    ref = torch.from_numpy(G["t5_qmask_out"])
+    assert_close(out, ref, None, max_abs=2e-5, min_cos=0.999999, what="t5_qmask")
+
+
 def test_deberta_layer_oracle_matches_reference():
     c = gi.deberta_layer_case()
     for key in ("hidden", "wq", "wk", "wv", "rel"):

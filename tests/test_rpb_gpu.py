@@ -117,6 +117,22 @@ def test_rpb_golden_reference_case():
     assert_close(out, ref, None, what="golden t5_enc")
 
 
+def test_rpb_golden_reference_case_query_varying_mask():
+    """The reference's own bias helper + SDPA on a [B, 1, L, L] mask (golden fixture) against
+    the query-row-mask kernel instance."""
+    G = np.load(gi.__file__.replace("golden_inputs.py", "golden.npz"))
+    c = gi.t5_case("t5_qmask")
+    op = _import_op()
+    dev = torch.device("cuda")
+    bf = torch.bfloat16
+    v = c["v"].to(bf)
+    out = op(c["q"].to(bf).to(dev), c["k"].to(bf).to(dev), v.to(dev), c["table"].to(bf).to(dev),
+             c["num_buckets"], c["max_distance"], False, c["mask"].to(bf).to(dev), 0.0, 1.0)
+    ref = torch.from_numpy(G["t5_qmask_out"])
+    gate = max(2e-2, 1.25 * 2 * 2.0 ** -8 * v.float().abs().max().item())   # see _check_qmask
+    assert_close(out, ref, None, max_abs=gate, what="golden t5_qmask")
+
+
 def test_rpb_c2_config_subset():
     # The C2 workload's shape (B=16, L=768, H=16, D=64, 32 buckets / 128) with ragged
     # lengths; the oracle checks two batch rows to bound CPU time.
