@@ -69,3 +69,20 @@ def test_gated_act_and_add_layer_norm_in_graphs():
     w, b = _rand(7, 1024) + 1.0, _rand(8, 1024, scale=0.1)
     _capture_and_check(lambda s: (_rand(s, 513, 1024), _rand(s + 10, 513, 1024)),
                        lambda x, r: fused_add_layer_norm(x, r, w, b, 1e-7))
+
+
+def test_deberta_fused_mode_in_graphs():
+    """The fused position mode (set-up kernel writing the workspace, then the attention
+    kernel) captured in a graph, workspace from the graph's memory pool: replays equal eager
+    calls bit for bit."""
+    from kernels.flash_deberta_attention import flash_deberta_attention, flash_deberta_attention_varlen
+    sl = torch.tensor([300, 170], dtype=torch.int32, device="cuda")
+    _capture_and_check(lambda s: tuple(_rand(s + i, *shape, scale=0.4 if i >= 3 else 1.0)
+                                       for i, shape in enumerate([(2, 4, 300, 64)] * 3 + [(1, 4, 512, 64)] * 2)),
+                       lambda q, k, v, rk, rq: flash_deberta_attention(q, k, v, sl, None, None, False, 0.07, 256, 512,
+                                                                       True, rel_key=rk, rel_query=rq))
+    cu = torch.tensor([0, 130, 131, 400], dtype=torch.int32, device="cuda")
+    _capture_and_check(lambda s: tuple(_rand(s + i, *shape, scale=0.4 if i >= 3 else 1.0)
+                                       for i, shape in enumerate([(400, 4, 64)] * 3 + [(1, 4, 512, 64)] * 2)),
+                       lambda q, k, v, rk, rq: flash_deberta_attention_varlen(q, k, v, cu, 269, None, None, False, 0.07,
+                                                                              256, 512, True, rel_key=rk, rel_query=rq))
